@@ -1,0 +1,490 @@
+"""Benchmark of the B200 backend on BASELINE.json's workloads.
+
+Headline (one JSON line on rank 0): the data-parallel MLP training step
+-- Linear 4096->16384, GELU, Linear 16384->4096, bf16,
+per-rank batch 8192, MSE loss, full backward and SGD -- run on N GPUs, one
+process per GPU (torchrun), gradients all-reduced over NCCL.  ``value`` is
+the whole-job throughput in samples/s (8192 * N samples per step), with the
+inputs already resident in HBM; ``e2e`` is the same step fed from pinned host
+memory every step (host->device copies and the loss read-back inside the
+timed region).  At N=1 rank 0 also reports the memory-bound operator sweep
+(config 2) and the GEMM set (config 3), and times the CPU port of the step
+(``cpu_baseline``).
+
+``--impl reference`` times the reference's CPU path of the same step (the
+oracle's port of it: tensorplay-mlu's host path is TensorPlay's CPU kernels,
+not installable here) on the host cores, rank 0 only.
+
+Usage:  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+PER_RANK_BATCH = 8192
+D_IN, D_HIDDEN = 4096, 16384
+METRIC = "dp_mlp_train_throughput"
+UNIT = "samples/s"
+WORKLOAD = "dp_mlp_4096x16384x4096_bf16_b8192_per_rank"
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), float(p["bf16_tflops_sustained"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def profile_figure(name: str, key: str):
+    """A number recorded in a committed ncu summary under profiles/ (``key: value``)."""
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        for line in open(path):
+            if line.strip().startswith(key + ":"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (SM clock, throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+        return False
+
+    def summary(self):
+        rows = []
+        for line in getattr(self, "lines", []):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags)
+                          if f.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------- distributed
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+class HostGroup:
+    """Host-side plumbing across ranks (gloo): barrier, max, store."""
+
+    def __init__(self, rank: int, world: int):
+        self.rank, self.world = rank, world
+        self.active = world > 1
+        if self.active:
+            import datetime
+            import torch.distributed as dist
+
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+            self.dist = dist
+            self.store = dist.distributed_c10d._get_default_store()
+
+    def barrier(self):
+        if self.active:
+            self.dist.barrier()
+
+    def max(self, value: float) -> float:
+        if not self.active:
+            return value
+        t = torch.tensor([value], dtype=torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.active:
+            self.dist.destroy_process_group()
+
+
+# ------------------------------------------------------------- reference arm
+
+def cpu_mlp_throughput(steps: int, warmup: int, rows: int = 16):
+    """The CPU port of the step (oracle/mlp.c) on `rows` sampled rows per step,
+    full-size weights, all host threads.  Returns (samples/s, threads, seconds)."""
+    import oracle as O
+    from tensorplay_mlu_b200.train import MLPConfig, init_params_host, make_batch_host
+
+    cfg = MLPConfig(d_in=D_IN, d_hidden=D_HIDDEN, batch=rows)
+    w1, b1, w2, b2 = [p.contiguous() for p in init_params_host(cfg, seed=0)]
+    x, t = make_batch_host(cfg, seed=0)
+    for _ in range(warmup):
+        O.mlp_step(x, t, w1, b1, w2, b2, cfg.lr)
+    start = time.perf_counter()
+    for _ in range(steps):
+        O.mlp_step(x, t, w1, b1, w2, b2, cfg.lr)
+    elapsed = time.perf_counter() - start
+    return rows * steps / elapsed, O.num_threads(), elapsed
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    rows = 16
+    value, threads, elapsed = cpu_mlp_throughput(args.steps, args.warmup, rows)
+    line = {
+        "impl": "reference",
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000.0 * elapsed / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "model": "MLP 4096-16384-4096 gelu, MSE, SGD",
+                   "global_batch": PER_RANK_BATCH * world, "parallelism": f"dp{world}"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{rows} rows per step of the 8192-row batch, full 134M-parameter "
+                                   "weights (forward, backward, SGD) -- oracle/mlp.c on the host cores"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------- our arm
+
+def time_events(fn, iters: int, warmup: int = 3) -> float:
+    """Mean milliseconds of `fn` over `iters`, CUDA events on the current stream."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(iters):
+        fn()
+    end.record()
+    end.synchronize()
+    return start.elapsed_time(end) / iters
+
+
+def op_sweep(ops, hbm_peak: float):
+    """memory-bound kernels, achieved GB/s and fraction of HBM."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    res = {}
+
+    def record(name, ms, nbytes):
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res[name] = {"ms": round(ms, 4), "gb_s": round(gbs, 1), "frac": round(gbs / hbm_peak, 3)}
+
+    M = N = 8192
+    for dt, tag in ((torch.float32, "f32"), (torch.bfloat16, "bf16")):
+        es = torch.finfo(dt).bits // 8
+        a = (torch.randn(M, N, generator=g, device="cuda") * 2).to(dt)
+        b = (torch.randn(N, generator=g, device="cuda") * 2).to(dt)
+        bpos = ops.add_Scalar(ops.abs(b), 1)
+        n = M * N
+        record(f"add_row_{tag}", time_events(lambda: ops.add_Tensor(a, b), 10), (2 * n + N) * es)
+        record(f"mul_row_{tag}", time_events(lambda: ops.mul_Tensor(a, b), 10), (2 * n + N) * es)
+        record(f"div_row_{tag}", time_events(lambda: ops.div_Tensor(a, bpos), 10), (2 * n + N) * es)
+        record(f"exp_{tag}", time_events(lambda: ops.exp(a), 10), 2 * n * es)
+        record(f"gelu_{tag}", time_events(lambda: ops.gelu(a), 10), 2 * n * es)
+        record(f"sigmoid_{tag}", time_events(lambda: ops.sigmoid(a), 10), 2 * n * es)
+        dy = torch.randn(M, N, generator=g, device="cuda").to(dt)
+        sy = ops.sigmoid(a)
+        record(f"gelu_backward_{tag}", time_events(lambda: ops.gelu_backward(dy, a), 10), 3 * n * es)
+        record(f"sigmoid_backward_{tag}", time_events(lambda: ops.sigmoid_backward(dy, sy), 10), 3 * n * es)
+        for name, fn in (("sum", ops.sum), ("mean", ops.mean)):
+            record(f"{name}_all_{tag}", time_events(lambda: fn(a), 10), n * es)
+        record(f"sum_dim-1_{tag}", time_events(lambda: ops.sum_dim_IntList(a, [-1]), 10), n * es + M * es)
+        record(f"amax_dim-1_{tag}", time_events(lambda: ops.amax(a, [-1]), 10), n * es + M * es)
+        record(f"amin_all_{tag}", time_events(lambda: ops.amin(a), 10), n * es)
+        del a, b, bpos, dy, sy
+        R, C = 32768, 4096
+        x = (torch.randn(R, C, generator=g, device="cuda") * 2).to(dt)
+        dx = torch.randn(R, C, generator=g, device="cuda").to(dt)
+        y = ops.softmax(x, -1)
+        ly = ops.log_softmax(x, -1)
+        m = R * C
+        record(f"softmax_{tag}", time_events(lambda: ops.softmax(x, -1), 10), 2 * m * es)
+        record(f"log_softmax_{tag}", time_events(lambda: ops.log_softmax(x, -1), 10), 2 * m * es)
+        record(f"softmax_backward_{tag}",
+               time_events(lambda: ops._softmax_backward_data(dx, y, -1, dt), 10), 3 * m * es)
+        record(f"log_softmax_backward_{tag}",
+               time_events(lambda: ops._log_softmax_backward_data(dx, ly, -1, dt), 10), 3 * m * es)
+        del x, dx, y, ly
+    ia = torch.randint(-1000000, 1000000, (M, N), generator=g, device="cuda", dtype=torch.int32)
+    ib = torch.randint(-1000000, 1000000, (M, N), generator=g, device="cuda", dtype=torch.int32)
+    record("add_int32", time_events(lambda: ops.add_Tensor(ia, ib), 10), 3 * M * N * 4)
+    record("amax_all_int32", time_events(lambda: ops.amax(ia), 10), M * N * 4)
+    del ia, ib
+    # The MLP's bias gradient: [8192, 16384] bf16 summed over dim 0.
+    hb = torch.randn(8192, 16384, generator=g, device="cuda").to(torch.bfloat16)
+    record("sum_dim0_8192x16384_bf16", time_events(lambda: ops.sum_dim_IntList(hb, [0]), 10),
+           (8192 * 16384 + 16384) * 2)
+    return res
+
+
+def gemm_set(ops, bf16_peak: float):
+    """achieved TFLOP/s of the GEMM shapes."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    res = {}
+
+    def rnd(*shape, k, dt=torch.bfloat16):
+        return (torch.randn(*shape, generator=g, device="cuda") * k ** -0.5).to(dt)
+
+    def record(name, ms, flops, peak):
+        tf = flops / (ms * 1e-3) / 1e12
+        res[name] = {"ms": round(ms, 4), "tflops": round(tf, 1), "frac": round(tf / peak, 3) if peak else None}
+
+    n = 8192
+    a, b = rnd(n, n, k=n), rnd(n, n, k=n)
+    record("mm_8192_bf16", time_events(lambda: ops.mm(a, b), 10), 2 * n ** 3, bf16_peak)
+    del a, b
+    M, K, N = 16384, 4096, 11008
+    x, w, bias = rnd(M, K, k=K), rnd(N, K, k=K), rnd(N, k=1)
+    wt = ops.contiguous(w.t())
+    record("addmm_16384x4096x11008_bf16", time_events(lambda: ops.addmm(bias, x, wt), 10), 2 * M * K * N,
+           bf16_peak)
+    record("linear_16384x4096x11008_bf16", time_events(lambda: ops.linear(x, w, bias), 10), 2 * M * K * N,
+           bf16_peak)
+    del x, w, bias, wt
+    ba, bb = rnd(64, 2048, 128, k=128), rnd(64, 128, 2048, k=128)
+    ms = time_events(lambda: ops.bmm(ba, bb), 10)
+    record("bmm_64x2048x128x2048_bf16", ms, 2 * 64 * 2048 * 128 * 2048, bf16_peak)
+    bytes_bmm = (64 * 2048 * 128 * 2 + 64 * 128 * 2048 + 64 * 2048 * 2048) * 2
+    res["bmm_64x2048x128x2048_bf16"]["hbm_gb_s"] = round(bytes_bmm / (ms * 1e-3) / 1e9, 1)
+    del ba, bb
+    n = 4096
+    fa, fb = rnd(n, n, k=n, dt=torch.float32), rnd(n, n, k=n, dt=torch.float32)
+    prev = torch.get_float32_matmul_precision()
+    torch.set_float32_matmul_precision("highest")
+    try:
+        simt_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+        record("mm_4096_fp32_highest", time_events(lambda: ops.mm(fa, fb), 5), 2 * n ** 3, simt_peak)
+        torch.set_float32_matmul_precision("high")
+        record("mm_4096_fp32_tf32", time_events(lambda: ops.mm(fa, fb), 10), 2 * n ** 3, bf16_peak / 2)
+    finally:
+        torch.set_float32_matmul_precision(prev)
+    return res
+
+
+def run_ours(args, rank: int, world: int, local: int) -> None:
+    torch.cuda.set_device(local)
+    import tensorplay_mlu_b200 as tpb
+    from tensorplay_mlu_b200 import _native as N
+    from tensorplay_mlu_b200 import distributed as D
+    from tensorplay_mlu_b200.train import DataParallelMLP, MLPConfig, init_params_host, make_batch_host
+
+    tpb.load()
+    ops = tpb.ops
+    host = HostGroup(rank, world)
+    hbm_peak, bf16_peak, bf16_sustained, peak_kind = peaks()
+    pg = D.create(_PrefixStore("nccl_b200", host.store), rank, world, device=local, timeout_s=300) \
+        if world > 1 else None
+
+    cfg = MLPConfig(d_in=D_IN, d_hidden=D_HIDDEN, batch=PER_RANK_BATCH)
+    model = DataParallelMLP(cfg, device=local, pg=pg, host_params=init_params_host(cfg, seed=0))
+    xh, th = make_batch_host(cfg, seed=rank)
+    x, t = ops.to_device(xh), ops.to_device(th)
+
+    # ---- device-resident timing (the headline value)
+    for _ in range(args.warmup):
+        model.step(x, t)
+    torch.cuda.synchronize()
+    host.barrier()
+    launches0 = N.lib().tp_b200_launch_count()
+    model.gemm_events = []
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        host.barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            loss = model.step(x, t)
+        end.record()
+        end.synchronize()
+        host.barrier()
+    launches = N.lib().tp_b200_launch_count() - launches0
+    ms_local = start.elapsed_time(end) / args.steps
+    ms = host.max(ms_local)
+    gemm_ms = [s.elapsed_time(e) for s, e in model.gemm_events]
+    model.gemm_events = None
+    gemm_avg_ms = sum(gemm_ms) / len(gemm_ms)
+    loss_value = ops.item(loss)
+
+    # ---- end to end: pinned host batches, copies and the loss read-back timed
+    xp, tp_ = xh.pin_memory(), th.pin_memory()
+    h2d = xp.numel() * xp.element_size() + tp_.numel() * tp_.element_size()
+    copy_stream = torch.cuda.Stream()
+    bufs = [(torch.empty_like(x), torch.empty_like(t)) for _ in range(2)]
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+
+    def upload(slot):
+        with torch.cuda.stream(copy_stream):
+            for dst, src in zip(bufs[slot], (xp, tp_)):
+                N.check(N.lib().tp_b200_memcpy(dst.data_ptr(), src.data_ptr(), src.numel() * src.element_size(),
+                                               1, local, -1, copy_stream.cuda_stream, 0), "h2d")
+            ev = torch.cuda.Event()
+            ev.record(copy_stream)
+        return ev
+
+    def e2e_steps(n):
+        ready = upload(0)
+        for i in range(n):
+            torch.cuda.current_stream().wait_event(ready)
+            xs, ts = bufs[i % 2]
+            if i + 1 < n:
+                copy_stream.wait_stream(torch.cuda.current_stream())
+                ready = upload((i + 1) % 2)
+            l = model.step(xs, ts)
+            l32 = ops._to_dtype(l, torch.float32)
+            N.check(N.lib().tp_b200_memcpy(loss_host.data_ptr(), l32.data_ptr(), 4, 2, local, -1,
+                                           N.stream_of(local), 1), "d2h")
+
+    e2e_steps(max(1, args.warmup // 2))
+    torch.cuda.synchronize()
+    host.barrier()
+    t0 = time.perf_counter()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    e2e_steps(args.steps)
+    e1.record()
+    e1.synchronize()
+    e2e_ms = host.max(e0.elapsed_time(e1) / args.steps)
+    host.barrier()
+
+    samples = PER_RANK_BATCH * world
+    value = samples / (ms * 1e-3)
+    e2e_value = samples / (e2e_ms * 1e-3)
+    gemm_flops = 2.0 * PER_RANK_BATCH * D_IN * D_HIDDEN
+    achieved = gemm_flops / (gemm_avg_ms * 1e-3) / 1e12
+    traffic = profile_figure("gemm_tc_mlp_8192x16384x4096.md", "dram_bytes_per_launch")
+
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: inputs/targets N(0,1) seeded by rank, nn.Linear-init weights seed 0",
+            "config": {"workload": WORKLOAD, "model": "MLP 4096-16384-4096 gelu, MSE loss, SGD lr 1e-3",
+                       "global_batch": samples, "per_rank_batch": PER_RANK_BATCH, "seq_len": None,
+                       "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (per-step working set ~1.9 GB > 126 MB)"},
+            "steps_per_s": round(1000.0 / ms, 2),
+            "step_tflops": round(model.flops_per_step() / (ms * 1e-3) / 1e12, 1),
+            "train_loss": loss_value,
+            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05, bf16 -> fp32)",
+                         "achieved": round(achieved, 1), "peak": bf16_sustained, "unit": "TFLOP/s",
+                         "frac": round(achieved / bf16_sustained, 3), "traffic": traffic,
+                         "peak_kind": f"{peak_kind} sustained bf16 (kernel timed inside a long step)",
+                         "per_launch_flops": gemm_flops, "avg_launch_ms": round(gemm_avg_ms, 4),
+                         "launches_timed": len(gemm_ms)},
+            "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 4),
+                    "path": "pinned host batch -> tp_b200_memcpy (copy stream, next batch prefetched) "
+                            "-> step -> loss -> tp_b200_memcpy to host"},
+            "gpu_launches": int(launches),
+            "clocks": clocks.summary(),
+        }
+    del x, t, bufs
+    if pg is not None:
+        torch.cuda.synchronize()
+        pg.destroy()
+    if rank == 0 and world == 1 and not args.no_extras:
+        del model
+        torch.cuda.empty_cache()
+        tpb.runtime.empty_cache()
+        line["op_sweep"] = op_sweep(ops, hbm_peak)
+        line["gemm_set"] = gemm_set(ops, bf16_peak)
+        cpu_value, threads, _ = cpu_mlp_throughput(2, 1, 16)
+        line["cpu_baseline"] = {"value": round(cpu_value, 2), "unit": UNIT, "cores": threads, "kind": "port",
+                                "sample": "16 rows per step of the 8192-row batch, full 134M-parameter weights, "
+                                          "2 timed steps after 1 warm-up (oracle/mlp.c, all host threads)"}
+        line["peaks"] = {"hbm_gbs": hbm_peak, "bf16_tflops": bf16_peak, "bf16_tflops_sustained": bf16_sustained,
+                         "kind": peak_kind}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    host.close()
+
+
+class _PrefixStore:
+    """Keys of the NCCL rendezvous under their own prefix in the job store."""
+
+    def __init__(self, prefix, store):
+        self.prefix, self.store = prefix, store
+
+    def set(self, key, value):
+        self.store.set(f"{self.prefix}/{key}", value)
+
+    def get(self, key, timeout=None):
+        return self.store.get(f"{self.prefix}/{key}")
+
+    def check(self, keys):
+        return self.store.check([f"{self.prefix}/{k}" for k in keys])
+
+
+def main() -> None:
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--no-extras", action="store_true", help="skip the op sweep, GEMM set and CPU baseline")
+    args = p.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

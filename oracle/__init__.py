@@ -1,0 +1,214 @@
+"""CPU oracle for the B200 backend's operators -- TEST INFRASTRUCTURE ONLY.
+
+Python face of ``oracle.c`` / ``mlp.c`` (see the header of oracle.c for what
+is restated from the reference and how it is pinned).  Only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline / reference arm
+may import this package, and only as the checker or the timed CPU path --
+never as part of the product.
+
+Inputs and outputs are host (CPU) torch tensors; any strides are accepted.
+Operator codes are the C ABI's (``include/tpb200.h``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIBRARY = os.path.join(HERE, "liboracle.so")
+MAX_DIMS = 8
+
+DTYPE_CODES = {
+    torch.uint8: 0, torch.int8: 1, torch.int16: 2, torch.int32: 3, torch.int64: 4,
+    torch.float16: 5, torch.float32: 6, torch.bfloat16: 7, torch.float64: 8, torch.bool: 9,
+}
+
+ADD, SUB, MUL, DIV, RSUB = range(5)
+(EXP, LOG, SQRT, RSQRT, NEG, ABS, POW, RELU, SIGMOID, TANH, SILU, GELU, GELU_TANH,
+ SQUARE) = range(14)
+(THRESHOLD_BACKWARD, SIGMOID_BACKWARD, TANH_BACKWARD, GELU_BACKWARD, GELU_TANH_BACKWARD,
+ SILU_BACKWARD) = range(6)
+SUM, MEAN, AMAX, AMIN = range(4)
+GEMM_ALLOW_TF32 = 1
+
+
+class _Desc(ctypes.Structure):
+    _fields_ = [
+        ("data", ctypes.c_void_p),
+        ("dtype", ctypes.c_int32),
+        ("ndim", ctypes.c_int32),
+        ("sizes", ctypes.c_int64 * MAX_DIMS),
+        ("strides", ctypes.c_int64 * MAX_DIMS),
+    ]
+
+
+def _d(t: torch.Tensor) -> _Desc:
+    assert t.device.type == "cpu", "the oracle works on host tensors"
+    d = _Desc()
+    d.data = t.data_ptr() if t.numel() else None
+    d.dtype = DTYPE_CODES[t.dtype]
+    d.ndim = t.dim()
+    for i, (s, st) in enumerate(zip(t.shape, t.stride())):
+        d.sizes[i] = s
+        d.strides[i] = st
+    return d
+
+
+_LIB = None
+
+
+def build() -> str:
+    """Compile liboracle.so (make -C oracle)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIBRARY
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is None:
+        if not os.path.isfile(LIBRARY):
+            build()
+        handle = ctypes.CDLL(LIBRARY)
+        T = ctypes.POINTER(_Desc)
+        D, I, I64 = ctypes.c_double, ctypes.c_int, ctypes.c_int64
+        sig = {
+            "orc_copy": [T, T],
+            "orc_fill": [T, D, I64],
+            "orc_binary": [I, T, T, T, D],
+            "orc_binary_scalar": [I, T, T, D, I64, D],
+            "orc_unary": [I, T, T, D],
+            "orc_unary_backward": [I, T, T, T, D],
+            "orc_reduce": [I, T, T, ctypes.c_uint32],
+            "orc_softmax": [I, T, T, I],
+            "orc_softmax_backward": [I, T, T, T, I],
+            "orc_gemm": [T, T, T, T, D, D, I],
+            "orc_gemm_sampled": [ctypes.c_void_p, ctypes.c_void_p, I64, T, T, T, D, D, I],
+            "orc_mlp_step": [I, I, I, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float,
+                             ctypes.POINTER(ctypes.c_float)],
+            "orc_num_threads": [],
+        }
+        for name, args in sig.items():
+            fn = getattr(handle, name)
+            fn.argtypes = args
+            fn.restype = ctypes.c_int
+        _LIB = handle
+    return _LIB
+
+
+def _ok(status: int, what: str) -> None:
+    if status != 0:
+        raise RuntimeError(f"oracle {what} failed ({status})")
+
+
+def copy(dst: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
+    _ok(lib().orc_copy(_d(dst), _d(src)), "copy")
+    return dst
+
+
+def cast(src: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    return copy(torch.empty(src.shape, dtype=dtype), src)
+
+
+def fill(dst: torch.Tensor, value) -> torch.Tensor:
+    if dst.dtype.is_floating_point:
+        _ok(lib().orc_fill(_d(dst), float(value), 0), "fill")
+    else:
+        _ok(lib().orc_fill(_d(dst), float(int(value)), int(value)), "fill")
+    return dst
+
+
+def binary(op: int, a: torch.Tensor, b: torch.Tensor, alpha=1.0) -> torch.Tensor:
+    assert a.dtype == b.dtype
+    out = torch.empty(torch.broadcast_shapes(a.shape, b.shape), dtype=a.dtype)
+    _ok(lib().orc_binary(op, _d(out), _d(a), _d(b), float(alpha)), "binary")
+    return out
+
+
+def binary_scalar(op: int, a: torch.Tensor, s, alpha=1.0) -> torch.Tensor:
+    out = torch.empty(a.shape, dtype=a.dtype)
+    si = int(s) if not a.dtype.is_floating_point else 0
+    _ok(lib().orc_binary_scalar(op, _d(out), _d(a), float(s), si, float(alpha)), "binary_scalar")
+    return out
+
+
+def unary(op: int, x: torch.Tensor, p: float = 0.0) -> torch.Tensor:
+    out = torch.empty(x.shape, dtype=x.dtype)
+    _ok(lib().orc_unary(op, _d(out), _d(x), float(p)), "unary")
+    return out
+
+
+def unary_backward(op: int, dy: torch.Tensor, z: torch.Tensor, p: float = 0.0) -> torch.Tensor:
+    out = torch.empty(dy.shape, dtype=dy.dtype)
+    _ok(lib().orc_unary_backward(op, _d(out), _d(dy), _d(z), float(p)), "unary_backward")
+    return out
+
+
+def reduce(op: int, x: torch.Tensor, dims, out_dtype: torch.dtype, keepdim: bool = False) -> torch.Tensor:
+    dims = [d % max(x.dim(), 1) for d in (dims if dims is not None else range(x.dim()))]
+    if not dims:
+        dims = list(range(x.dim()))
+    mask = 0
+    for d in dims:
+        mask |= 1 << d
+    keep = [1 if (mask >> i) & 1 else s for i, s in enumerate(x.shape)]
+    out = torch.empty(keep, dtype=out_dtype)
+    _ok(lib().orc_reduce(op, _d(out), _d(x), mask), "reduce")
+    if keepdim:
+        return out
+    return out.reshape([s for i, s in enumerate(x.shape) if not (mask >> i) & 1])
+
+
+def softmax(x: torch.Tensor, dim: int, log: bool = False) -> torch.Tensor:
+    x = x.contiguous()
+    out = torch.empty(x.shape, dtype=x.dtype)
+    _ok(lib().orc_softmax(int(log), _d(out), _d(x), dim), "softmax")
+    return out
+
+
+def softmax_backward(dy: torch.Tensor, y: torch.Tensor, dim: int, log: bool = False) -> torch.Tensor:
+    dy, y = dy.contiguous(), y.contiguous()
+    out = torch.empty(dy.shape, dtype=dy.dtype)
+    _ok(lib().orc_softmax_backward(int(log), _d(out), _d(dy), _d(y), dim), "softmax_backward")
+    return out
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, c=None, alpha=1.0, beta=0.0, flags: int = 0) -> torch.Tensor:
+    shape = list(a.shape[:-1]) + [b.shape[-1]]
+    if a.dim() == 3:
+        shape[0] = max(a.shape[0], b.shape[0])
+    out = torch.empty(shape, dtype=a.dtype)
+    _ok(lib().orc_gemm(_d(out), _d(a), _d(b), _d(c) if c is not None else None, float(alpha),
+                       float(beta), flags), "gemm")
+    return out
+
+
+def gemm_sampled(a: torch.Tensor, b: torch.Tensor, idx: np.ndarray, c=None, alpha=1.0, beta=0.0,
+                 flags: int = 0) -> np.ndarray:
+    """alpha * (a @ b) + beta * c at the (batch, m, n) rows of ``idx``, in float64."""
+    idx = np.ascontiguousarray(idx, dtype=np.int64)
+    vals = np.empty(idx.shape[0], dtype=np.float64)
+    _ok(lib().orc_gemm_sampled(vals.ctypes.data, idx.ctypes.data, idx.shape[0], _d(a), _d(b),
+                               _d(c) if c is not None else None, float(alpha), float(beta), flags),
+        "gemm_sampled")
+    return vals
+
+
+def mlp_step(x, t, w1, b1, w2, b2, lr: float) -> float:
+    """One SGD step of the BASELINE MLP on bf16 host tensors (weights updated in place)."""
+    for tensor in (x, t, w1, b1, w2, b2):
+        assert tensor.dtype == torch.bfloat16 and tensor.is_contiguous()
+    loss = ctypes.c_float()
+    _ok(lib().orc_mlp_step(x.shape[0], x.shape[1], w1.shape[0], x.data_ptr(), t.data_ptr(),
+                           w1.data_ptr(), b1.data_ptr(), w2.data_ptr(), b2.data_ptr(), float(lr),
+                           ctypes.byref(loss)), "mlp_step")
+    return loss.value
+
+
+def num_threads() -> int:
+    return lib().orc_num_threads()

@@ -1,0 +1,590 @@
+/*
+ * oracle.c -- CPU restatement of the operator semantics the B200 backend
+ * claims.  TEST INFRASTRUCTURE ONLY: it is the checker of the CUDA path
+ * (tests/, __graft_entry__.smoke(), bench.py's cpu_baseline / reference arm)
+ * and is never linked into or called by the product library.
+ *
+ * What it restates.  tensorplay-mlu's host path is TensorPlay's own CPU kernels
+ * (every claimed operator falls back to them for integers and float64,
+ * tensorplay_mlu/csrc/BinaryKernels.cpp:148-151 and siblings); TensorPlay is
+ * not installed here and its device arithmetic is inside the closed CNNL
+ * library, so neither can be run.  This file restates the semantics those
+ * kernels share (ATen-compatible operator schemas) from the reference's call
+ * sites:
+ *   - broadcasting and dtype handling: tensorplay_mlu/csrc/Cnnl.cpp:178-205;
+ *   - add/sub with alpha, true division: BinaryKernels.cpp:44-87 (CNNL
+ *     OpTensor ADD with alpha2 = +-alpha, cnnlDiv_v3 DIV_TRUE);
+ *   - scalar forms as y = alpha*x + beta: BinaryKernels.cpp:204-248
+ *     (restated as x (op) s -- mathematically the same, without the
+ *     reference's float truncation of alpha and beta);
+ *   - unary math, pow special cases, activations (exact / tanh gelu) and their
+ *     backward formulas: UnaryKernels.cpp:48-287;
+ *   - reductions with keepdim then view: ReduceKernels.cpp:21-95;
+ *   - max-subtracted softmax / log_softmax and their backward over
+ *     [outer, dim, inner]: ReduceKernels.cpp:146-199;
+ *   - C = alpha*A@B + beta*C with transposed operands: BlasKernels.cpp:202-242;
+ *   - casts: CopyKernels.cpp:42-220 (16-bit floats through fp32,
+ *     float -> int truncation, != 0 for bool).
+ * Arithmetic: floating values in double (one rounding to the output dtype at
+ * the end, so the oracle is at least as accurate as any fp32 kernel),
+ * integers in int64 wrapped to the dtype -- bit-exact for integer work.
+ *
+ * Pinning: against PyTorch 2.11 CPU outputs (same operator schemas) committed
+ * as fixtures under tests/golden/ with the script that made them, and against
+ * the exact-valued cases of the reference's own tests (round trips, x*3+1,
+ * single-rank collectives).  TensorPlay's CPU kernels themselves are absent,
+ * so float parity against them is pinned only through that stand-in.
+ *
+ * Build: see oracle/Makefile (gcc -O2 -fopenmp -shared).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "tpb200.h"
+
+/* ------------------------------------------------------------ scalars -- */
+
+static float bits_to_float(uint32_t u) {
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+static uint32_t float_to_bits(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    return u;
+}
+
+/* bfloat16 = the high 16 bits of an IEEE single; round to nearest even. */
+static float bf16_to_float(uint16_t h) { return bits_to_float((uint32_t)h << 16); }
+static uint16_t float_to_bf16(float f) {
+    uint32_t u = float_to_bits(f);
+    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu)) return (uint16_t)((u >> 16) | 0x40);
+    const uint32_t lsb = (u >> 16) & 1u;
+    u += 0x7fffu + lsb;
+    return (uint16_t)(u >> 16);
+}
+
+/* IEEE half <-> single, round to nearest even (including subnormals). */
+static float half_to_float(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    const uint32_t exp = (h >> 10) & 0x1f;
+    const uint32_t man = h & 0x3ff;
+    if (exp == 0) {
+        if (man == 0) return bits_to_float(sign);
+        float v = (float)man / 1024.0f / 16384.0f; /* man * 2^-24 */
+        return sign ? -v : v;
+    }
+    if (exp == 31) return bits_to_float(sign | 0x7f800000u | (man << 13));
+    return bits_to_float(sign | ((exp + 112) << 23) | (man << 13));
+}
+static uint16_t float_to_half(float f) {
+    const uint32_t u = float_to_bits(f);
+    const uint16_t sign = (uint16_t)((u >> 16) & 0x8000u);
+    const int32_t exp = (int32_t)((u >> 23) & 0xff);
+    uint32_t man = u & 0x7fffff;
+    if (exp == 0xff) return (uint16_t)(sign | 0x7c00u | (man ? 0x200u : 0));
+    const int32_t e = exp - 127 + 15;
+    if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+    if (e <= 0) {
+        if (e < -10) return sign;
+        man |= 0x800000u;
+        const int shift = 14 - e;
+        uint32_t q = man >> shift;
+        const uint32_t rem = man & ((1u << shift) - 1);
+        const uint32_t half = 1u << (shift - 1);
+        if (rem > half || (rem == half && (q & 1))) q++;
+        return (uint16_t)(sign | q);
+    }
+    uint32_t q = ((uint32_t)e << 10) | (man >> 13);
+    const uint32_t rem = man & 0x1fff;
+    if (rem > 0x1000 || (rem == 0x1000 && (q & 1))) q++;
+    return (uint16_t)(sign | q);
+}
+
+static int is_float_dtype(int d) { return d == TPB_F16 || d == TPB_F32 || d == TPB_BF16 || d == TPB_F64; }
+
+static size_t esize(int d) {
+    switch (d) {
+        case TPB_U8: case TPB_I8: case TPB_BOOL: return 1;
+        case TPB_I16: case TPB_F16: case TPB_BF16: return 2;
+        case TPB_I32: case TPB_F32: return 4;
+        default: return 8;
+    }
+}
+
+/* Element access: floating values as double, integer values as int64. */
+static double loadf(const tpb_tensor* t, int64_t off) {
+    const char* p = (const char*)t->data + off * (int64_t)esize(t->dtype);
+    switch (t->dtype) {
+        case TPB_F32: return *(const float*)p;
+        case TPB_F64: return *(const double*)p;
+        case TPB_F16: return half_to_float(*(const uint16_t*)p);
+        case TPB_BF16: return bf16_to_float(*(const uint16_t*)p);
+        case TPB_U8: return *(const uint8_t*)p;
+        case TPB_I8: return *(const int8_t*)p;
+        case TPB_I16: return *(const int16_t*)p;
+        case TPB_I32: return *(const int32_t*)p;
+        case TPB_I64: return (double)*(const int64_t*)p;
+        default: return *(const uint8_t*)p ? 1.0 : 0.0;
+    }
+}
+static int64_t loadi(const tpb_tensor* t, int64_t off) {
+    const char* p = (const char*)t->data + off * (int64_t)esize(t->dtype);
+    switch (t->dtype) {
+        case TPB_U8: return *(const uint8_t*)p;
+        case TPB_I8: return *(const int8_t*)p;
+        case TPB_I16: return *(const int16_t*)p;
+        case TPB_I32: return *(const int32_t*)p;
+        case TPB_I64: return *(const int64_t*)p;
+        case TPB_BOOL: return *(const uint8_t*)p ? 1 : 0;
+        default: return (int64_t)loadf(t, off); /* float -> int truncates */
+    }
+}
+/* Store a double into any dtype: 16-bit floats via fp32, ints truncate. */
+static void storef(const tpb_tensor* t, int64_t off, double v) {
+    char* p = (char*)t->data + off * (int64_t)esize(t->dtype);
+    switch (t->dtype) {
+        case TPB_F32: *(float*)p = (float)v; break;
+        case TPB_F64: *(double*)p = v; break;
+        case TPB_F16: *(uint16_t*)p = float_to_half((float)v); break;
+        case TPB_BF16: *(uint16_t*)p = float_to_bf16((float)v); break;
+        case TPB_BOOL: *(uint8_t*)p = v != 0.0; break;
+        case TPB_U8: *(uint8_t*)p = (uint8_t)(int64_t)v; break;
+        case TPB_I8: *(int8_t*)p = (int8_t)(int64_t)v; break;
+        case TPB_I16: *(int16_t*)p = (int16_t)(int64_t)v; break;
+        case TPB_I32: *(int32_t*)p = (int32_t)(int64_t)v; break;
+        default: *(int64_t*)p = (int64_t)v; break;
+    }
+}
+static void storei(const tpb_tensor* t, int64_t off, int64_t v) {
+    char* p = (char*)t->data + off * (int64_t)esize(t->dtype);
+    switch (t->dtype) {
+        case TPB_U8: *(uint8_t*)p = (uint8_t)v; break;
+        case TPB_I8: *(int8_t*)p = (int8_t)v; break;
+        case TPB_I16: *(int16_t*)p = (int16_t)v; break;
+        case TPB_I32: *(int32_t*)p = (int32_t)v; break;
+        case TPB_I64: *(int64_t*)p = v; break;
+        case TPB_BOOL: *(uint8_t*)p = v != 0; break;
+        default: storef(t, off, (double)v); break;
+    }
+}
+
+/* ------------------------------------------------------------ shapes -- */
+
+static int64_t numel(const tpb_tensor* t) {
+    int64_t n = 1;
+    for (int i = 0; i < t->ndim; ++i) n *= t->sizes[i];
+    return n;
+}
+
+/* Strides of `t` seen at `out`'s shape (right-aligned broadcasting). */
+static int bstrides(const tpb_tensor* t, const tpb_tensor* out, int64_t* st) {
+    const int off = out->ndim - t->ndim;
+    if (off < 0) return -1;
+    for (int i = 0; i < out->ndim; ++i) {
+        if (i < off) { st[i] = 0; continue; }
+        const int64_t s = t->sizes[i - off];
+        if (s != out->sizes[i] && s != 1) return -1;
+        st[i] = (s == 1) ? 0 : t->strides[i - off];
+    }
+    return 0;
+}
+
+/* Offset of linear index `i` (row-major over `sizes`) with strides `st`. */
+static int64_t offset_of(int64_t i, int ndim, const int64_t* sizes, const int64_t* st) {
+    int64_t off = 0;
+    for (int d = ndim - 1; d >= 0; --d) {
+        const int64_t q = i / sizes[d];
+        off += (i - q * sizes[d]) * st[d];
+        i = q;
+    }
+    return off;
+}
+
+/* ----------------------------------------------------------- elementwise -- */
+
+static double binf(int op, double a, double b, double alpha) {
+    switch (op) {
+        case TPB_ADD: return a + alpha * b;
+        case TPB_SUB: return a - alpha * b;
+        case TPB_MUL: return a * b;
+        case TPB_DIV: return a / b;
+        default: return b - alpha * a;
+    }
+}
+static int64_t bini(int op, int64_t a, int64_t b, int64_t alpha) {
+    /* two's-complement wrap: compute in uint64 */
+    const uint64_t ua = (uint64_t)a, ub = (uint64_t)b, ual = (uint64_t)alpha;
+    switch (op) {
+        case TPB_ADD: return (int64_t)(ua + ual * ub);
+        case TPB_SUB: return (int64_t)(ua - ual * ub);
+        case TPB_MUL: return (int64_t)(ua * ub);
+        case TPB_DIV: return b == 0 ? 0 : a / b;
+        default: return (int64_t)(ub - ual * ua);
+    }
+}
+
+int orc_copy(const tpb_tensor* dst, const tpb_tensor* src) {
+    int64_t st[TPB_MAX_DIMS], sd[TPB_MAX_DIMS];
+    if (bstrides(src, dst, st)) return -1;
+    for (int i = 0; i < dst->ndim; ++i) sd[i] = dst->strides[i];
+    const int64_t n = numel(dst);
+    const int fsrc = is_float_dtype(src->dtype);
+#pragma omp parallel for schedule(static) if (n > 65536)
+    for (int64_t i = 0; i < n; ++i) {
+        const int64_t od = offset_of(i, dst->ndim, dst->sizes, sd);
+        const int64_t os = offset_of(i, dst->ndim, dst->sizes, st);
+        if (fsrc) storef(dst, od, loadf(src, os));
+        else storei(dst, od, loadi(src, os));
+    }
+    return 0;
+}
+
+int orc_fill(const tpb_tensor* dst, double v, int64_t iv) {
+    const int64_t n = numel(dst);
+    for (int64_t i = 0; i < n; ++i) {
+        const int64_t od = offset_of(i, dst->ndim, dst->sizes, dst->strides);
+        if (is_float_dtype(dst->dtype)) storef(dst, od, v);
+        else storei(dst, od, iv);
+    }
+    return 0;
+}
+
+int orc_binary(int op, const tpb_tensor* out, const tpb_tensor* a, const tpb_tensor* b, double alpha) {
+    int64_t sa[TPB_MAX_DIMS], sb[TPB_MAX_DIMS];
+    if (bstrides(a, out, sa) || bstrides(b, out, sb)) return -1;
+    const int64_t n = numel(out);
+    const int fl = is_float_dtype(out->dtype);
+#pragma omp parallel for schedule(static) if (n > 65536)
+    for (int64_t i = 0; i < n; ++i) {
+        const int64_t oo = offset_of(i, out->ndim, out->sizes, out->strides);
+        const int64_t oa = offset_of(i, out->ndim, out->sizes, sa);
+        const int64_t ob = offset_of(i, out->ndim, out->sizes, sb);
+        if (fl) storef(out, oo, binf(op, loadf(a, oa), loadf(b, ob), alpha));
+        else storei(out, oo, bini(op, loadi(a, oa), loadi(b, ob), (int64_t)alpha));
+    }
+    return 0;
+}
+
+int orc_binary_scalar(int op, const tpb_tensor* out, const tpb_tensor* a, double s, int64_t si,
+                      double alpha) {
+    int64_t sa[TPB_MAX_DIMS];
+    if (bstrides(a, out, sa)) return -1;
+    const int64_t n = numel(out);
+    const int fl = is_float_dtype(out->dtype);
+#pragma omp parallel for schedule(static) if (n > 65536)
+    for (int64_t i = 0; i < n; ++i) {
+        const int64_t oo = offset_of(i, out->ndim, out->sizes, out->strides);
+        const int64_t oa = offset_of(i, out->ndim, out->sizes, sa);
+        if (fl) storef(out, oo, binf(op, loadf(a, oa), s, alpha));
+        else storei(out, oo, bini(op, loadi(a, oa), si, (int64_t)alpha));
+    }
+    return 0;
+}
+
+static double pow_special(double x, double p) {
+    if (p == 2.0) return x * x;
+    if (p == 1.0) return x;
+    if (p == 0.0) return 1.0;
+    if (p == 3.0) return x * x * x;
+    if (p == 0.5) return sqrt(x);
+    if (p == -0.5) return 1.0 / sqrt(x);
+    if (p == -1.0) return 1.0 / x;
+    if (p == -2.0) return 1.0 / (x * x);
+    return pow(x, p);
+}
+
+static double unf(int op, double x, double p) {
+    switch (op) {
+        case TPB_EXP: return exp(x);
+        case TPB_LOG: return log(x);
+        case TPB_SQRT: return sqrt(x);
+        case TPB_RSQRT: return 1.0 / sqrt(x);
+        case TPB_NEG: return -x;
+        case TPB_ABS: return fabs(x);
+        case TPB_POW: return pow_special(x, p);
+        case TPB_RELU: return (x > 0 || x != x) ? x : 0.0;
+        case TPB_SIGMOID: return 1.0 / (1.0 + exp(-x));
+        case TPB_TANH: return tanh(x);
+        case TPB_SILU: return x / (1.0 + exp(-x));
+        case TPB_GELU: return 0.5 * x * (1.0 + erf(x * 0.70710678118654752440));
+        case TPB_GELU_TANH: {
+            const double inner = 0.79788456080286535588 * (x + 0.044715 * x * x * x);
+            return 0.5 * x * (1.0 + tanh(inner));
+        }
+        default: return x * x;
+    }
+}
+static int64_t uni(int op, int64_t x, double p) {
+    switch (op) {
+        case TPB_NEG: return (int64_t)(0 - (uint64_t)x);
+        case TPB_ABS: return x < 0 ? (int64_t)(0 - (uint64_t)x) : x;
+        case TPB_RELU: return x > 0 ? x : 0;
+        case TPB_SQUARE: return (int64_t)((uint64_t)x * (uint64_t)x);
+        default: {
+            uint64_t r = 1, b = (uint64_t)x;
+            for (int64_t e = (int64_t)p; e > 0; e >>= 1) {
+                if (e & 1) r *= b;
+                b *= b;
+            }
+            return (int64_t)r;
+        }
+    }
+}
+
+int orc_unary(int op, const tpb_tensor* out, const tpb_tensor* x, double p) {
+    const int64_t n = numel(out);
+    const int fl = is_float_dtype(out->dtype);
+#pragma omp parallel for schedule(static) if (n > 65536)
+    for (int64_t i = 0; i < n; ++i) {
+        const int64_t oo = offset_of(i, out->ndim, out->sizes, out->strides);
+        const int64_t ox = offset_of(i, x->ndim, x->sizes, x->strides);
+        if (fl) storef(out, oo, unf(op, loadf(x, ox), p));
+        else storei(out, oo, uni(op, loadi(x, ox), p));
+    }
+    return 0;
+}
+
+static double ubf(int op, double dy, double z, double p) {
+    switch (op) {
+        case TPB_THRESHOLD_BACKWARD: return z <= p ? 0.0 : dy;
+        case TPB_SIGMOID_BACKWARD: return dy * (1.0 - z) * z;
+        case TPB_TANH_BACKWARD: return dy * (1.0 - z * z);
+        case TPB_GELU_BACKWARD: {
+            const double cdf = 0.5 * (1.0 + erf(z * 0.70710678118654752440));
+            const double pdf = exp(-0.5 * z * z) * 0.39894228040143267794;
+            return dy * (cdf + z * pdf);
+        }
+        case TPB_GELU_TANH_BACKWARD: {
+            const double kb = 0.79788456080286535588, kk = 0.044715;
+            const double x2 = z * z;
+            const double t = tanh(kb * (z + kk * x2 * z));
+            const double left = 0.5 * z, right = 1.0 + t;
+            return dy * (0.5 * right + left * (1.0 - t * t) * kb * (1.0 + 3.0 * kk * x2));
+        }
+        default: {
+            const double s = 1.0 / (1.0 + exp(-z));
+            return dy * s * (1.0 + z * (1.0 - s));
+        }
+    }
+}
+
+int orc_unary_backward(int op, const tpb_tensor* dx, const tpb_tensor* dy, const tpb_tensor* z, double p) {
+    const int64_t n = numel(dx);
+    const int fl = is_float_dtype(dx->dtype);
+#pragma omp parallel for schedule(static) if (n > 65536)
+    for (int64_t i = 0; i < n; ++i) {
+        const int64_t o0 = offset_of(i, dx->ndim, dx->sizes, dx->strides);
+        const int64_t o1 = offset_of(i, dy->ndim, dy->sizes, dy->strides);
+        const int64_t o2 = offset_of(i, z->ndim, z->sizes, z->strides);
+        if (fl) storef(dx, o0, ubf(op, loadf(dy, o1), loadf(z, o2), p));
+        else storei(dx, o0, (op == TPB_THRESHOLD_BACKWARD && loadi(z, o2) <= (int64_t)p) ? 0 : loadi(dy, o1));
+    }
+    return 0;
+}
+
+/* ----------------------------------------------------------- reductions -- */
+
+int orc_reduce(int op, const tpb_tensor* out, const tpb_tensor* x, uint32_t mask) {
+    if (out->ndim != x->ndim) return -1;
+    const int nd = x->ndim;
+    int64_t rsizes[TPB_MAX_DIMS], rstr[TPB_MAX_DIMS], ksizes[TPB_MAX_DIMS], kstr[TPB_MAX_DIMS];
+    int nr = 0, nk = 0;
+    for (int i = 0; i < nd; ++i) {
+        if ((mask >> i) & 1) { rsizes[nr] = x->sizes[i]; rstr[nr++] = x->strides[i]; }
+        else { ksizes[nk] = x->sizes[i]; kstr[nk++] = x->strides[i]; }
+    }
+    int64_t R = 1, K = 1;
+    for (int i = 0; i < nr; ++i) R *= rsizes[i];
+    for (int i = 0; i < nk; ++i) K *= ksizes[i];
+    const int fl = is_float_dtype(x->dtype);
+    const int fout = is_float_dtype(out->dtype);
+#pragma omp parallel for schedule(static) if (K > 16)
+    for (int64_t k = 0; k < K; ++k) {
+        const int64_t base = offset_of(k, nk, ksizes, kstr);
+        double accf = op == TPB_AMAX ? -INFINITY : op == TPB_AMIN ? INFINITY : 0.0;
+        int64_t acci = op == TPB_AMAX ? INT64_MIN : op == TPB_AMIN ? INT64_MAX : 0;
+        int nan = 0;
+        for (int64_t r = 0; r < R; ++r) {
+            const int64_t off = base + offset_of(r, nr, rsizes, rstr);
+            if (fl) {
+                const double v = loadf(x, off);
+                if (v != v) nan = 1;
+                if (op == TPB_AMAX) accf = v > accf ? v : accf;
+                else if (op == TPB_AMIN) accf = v < accf ? v : accf;
+                else accf += v;
+            } else {
+                const int64_t v = loadi(x, off);
+                if (op == TPB_AMAX) acci = v > acci ? v : acci;
+                else if (op == TPB_AMIN) acci = v < acci ? v : acci;
+                else acci = (int64_t)((uint64_t)acci + (uint64_t)v);
+            }
+        }
+        if (nan && (op == TPB_AMAX || op == TPB_AMIN)) accf = NAN;
+        /* out is keepdim-shaped and contiguous: its k-th element */
+        if (fl) {
+            if (op == TPB_MEAN) accf /= (double)R;
+            storef(out, k, accf);
+        } else if (op == TPB_MEAN) {
+            storef(out, k, (double)acci / (double)R);
+        } else if (fout) {
+            storef(out, k, (double)acci);
+        } else {
+            storei(out, k, acci);
+        }
+    }
+    return 0;
+}
+
+static void softmax_geometry(const tpb_tensor* t, int dim, int64_t* outer, int64_t* D, int64_t* inner) {
+    const int nd = t->ndim == 0 ? 1 : t->ndim;
+    if (dim < 0) dim += nd;
+    *outer = 1;
+    *inner = 1;
+    *D = t->ndim == 0 ? 1 : t->sizes[dim];
+    for (int i = 0; i < dim; ++i) *outer *= t->sizes[i];
+    for (int i = dim + 1; i < t->ndim; ++i) *inner *= t->sizes[i];
+}
+
+/* Inputs and outputs are contiguous for the softmax family. */
+int orc_softmax(int log_, const tpb_tensor* out, const tpb_tensor* x, int dim) {
+    int64_t outer, D, inner;
+    softmax_geometry(x, dim, &outer, &D, &inner);
+#pragma omp parallel for schedule(static) if (outer * inner > 16)
+    for (int64_t t = 0; t < outer * inner; ++t) {
+        const int64_t o = t / inner, i = t % inner;
+        const int64_t base = o * D * inner + i;
+        double m = -INFINITY;
+        for (int64_t d = 0; d < D; ++d) {
+            const double v = loadf(x, base + d * inner);
+            if (v > m || v != v) m = v;
+        }
+        double s = 0.0;
+        for (int64_t d = 0; d < D; ++d) s += exp(loadf(x, base + d * inner) - m);
+        for (int64_t d = 0; d < D; ++d) {
+            const double v = loadf(x, base + d * inner);
+            storef(out, base + d * inner, log_ ? v - m - log(s) : exp(v - m) / s);
+        }
+    }
+    return 0;
+}
+
+int orc_softmax_backward(int log_, const tpb_tensor* dx, const tpb_tensor* dy, const tpb_tensor* y, int dim) {
+    int64_t outer, D, inner;
+    softmax_geometry(dy, dim, &outer, &D, &inner);
+#pragma omp parallel for schedule(static) if (outer * inner > 16)
+    for (int64_t t = 0; t < outer * inner; ++t) {
+        const int64_t o = t / inner, i = t % inner;
+        const int64_t base = o * D * inner + i;
+        double acc = 0.0;
+        for (int64_t d = 0; d < D; ++d) {
+            const double g = loadf(dy, base + d * inner);
+            acc += log_ ? g : g * loadf(y, base + d * inner);
+        }
+        for (int64_t d = 0; d < D; ++d) {
+            const double g = loadf(dy, base + d * inner), w = loadf(y, base + d * inner);
+            storef(dx, base + d * inner, log_ ? g - exp(w) * acc : w * (g - acc));
+        }
+    }
+    return 0;
+}
+
+/* ----------------------------------------------------------------- GEMM -- */
+
+/* Round an fp32 value to TF32 (10 explicit mantissa bits, nearest-even). */
+static double tf32_round(double v) {
+    uint32_t u = float_to_bits((float)v);
+    if ((u & 0x7f800000u) == 0x7f800000u) return v;
+    u += 0xfffu + ((u >> 13) & 1u);
+    u &= 0xffffe000u;
+    return bits_to_float(u);
+}
+
+/* out[b][m][n] = alpha * sum_k a[b][m][k] b[b][k][n] + beta * c (broadcast),
+ * accumulated in double (int64 for integer types). */
+int orc_gemm(const tpb_tensor* out, const tpb_tensor* a, const tpb_tensor* b, const tpb_tensor* c,
+             double alpha, double beta, int flags) {
+    const int nd = out->ndim;
+    const int64_t M = out->sizes[nd - 2], N = out->sizes[nd - 1], K = a->sizes[nd - 1];
+    const int64_t B = nd == 3 ? out->sizes[0] : 1;
+    const int64_t sab = nd == 3 && a->sizes[0] != 1 ? a->strides[0] : 0;
+    const int64_t sbb = nd == 3 && b->sizes[0] != 1 ? b->strides[0] : 0;
+    int64_t sc[TPB_MAX_DIMS] = {0};
+    const int use_c = c != NULL && beta != 0.0;
+    if (use_c && bstrides(c, out, sc)) return -1;
+    const int fl = is_float_dtype(out->dtype);
+    const int tf32 = (flags & TPB_GEMM_ALLOW_TF32) && out->dtype == TPB_F32;
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int64_t bb = 0; bb < B; ++bb) {
+        for (int64_t m = 0; m < M; ++m) {
+            for (int64_t n = 0; n < N; ++n) {
+                const int64_t oo = (nd == 3 ? bb * out->strides[0] : 0) + m * out->strides[nd - 2] +
+                                   n * out->strides[nd - 1];
+                if (fl) {
+                    double acc = 0.0;
+                    for (int64_t k = 0; k < K; ++k) {
+                        double x = loadf(a, bb * sab + m * a->strides[nd - 2] + k * a->strides[nd - 1]);
+                        double y = loadf(b, bb * sbb + k * b->strides[nd - 2] + n * b->strides[nd - 1]);
+                        if (tf32) { x = tf32_round(x); y = tf32_round(y); }
+                        acc += x * y;
+                    }
+                    double v = alpha * acc;
+                    if (use_c) v += beta * loadf(c, (nd == 3 ? bb * sc[0] : 0) + m * sc[nd - 2] + n * sc[nd - 1]);
+                    storef(out, oo, v);
+                } else {
+                    uint64_t acc = 0;
+                    for (int64_t k = 0; k < K; ++k) {
+                        acc += (uint64_t)loadi(a, bb * sab + m * a->strides[nd - 2] + k * a->strides[nd - 1]) *
+                               (uint64_t)loadi(b, bb * sbb + k * b->strides[nd - 2] + n * b->strides[nd - 1]);
+                    }
+                    uint64_t v = (uint64_t)(int64_t)alpha * acc;
+                    if (use_c) v += (uint64_t)(int64_t)beta *
+                                    (uint64_t)loadi(c, (nd == 3 ? bb * sc[0] : 0) + m * sc[nd - 2] + n * sc[nd - 1]);
+                    storei(out, oo, (int64_t)v);
+                }
+            }
+        }
+    }
+    return 0;
+}
+
+/* Selected outputs only (for problems too large to recompute in full):
+ * idx holds `count` (batch, m, n) triples; vals receives alpha*acc + beta*c in
+ * double, before any rounding to the output dtype. */
+int orc_gemm_sampled(double* vals, const int64_t* idx, int64_t count, const tpb_tensor* a,
+                     const tpb_tensor* b, const tpb_tensor* c, double alpha, double beta, int flags) {
+    const int nd = a->ndim;
+    const int64_t K = a->sizes[nd - 1];
+    const int64_t sab = nd == 3 && a->sizes[0] != 1 ? a->strides[0] : 0;
+    const int64_t sbb = nd == 3 && b->sizes[0] != 1 ? b->strides[0] : 0;
+    const int tf32 = (flags & TPB_GEMM_ALLOW_TF32) && a->dtype == TPB_F32;
+    int64_t sc[TPB_MAX_DIMS] = {0};
+    const int use_c = c != NULL && beta != 0.0;
+    tpb_tensor shape;
+    if (use_c) {
+        /* broadcast c against [.., M, N]; only its own strides matter */
+        shape.ndim = nd;
+        for (int i = 0; i < nd; ++i) shape.sizes[i] = 1 << 30;
+        const int off = nd - c->ndim;
+        for (int i = 0; i < nd; ++i) sc[i] = (i < off || c->sizes[i - off] == 1) ? 0 : c->strides[i - off];
+    }
+#pragma omp parallel for schedule(static)
+    for (int64_t s = 0; s < count; ++s) {
+        const int64_t bb = idx[3 * s], m = idx[3 * s + 1], n = idx[3 * s + 2];
+        double acc = 0.0;
+        for (int64_t k = 0; k < K; ++k) {
+            double x = loadf(a, bb * sab + m * a->strides[nd - 2] + k * a->strides[nd - 1]);
+            double y = loadf(b, bb * sbb + k * b->strides[nd - 2] + n * b->strides[nd - 1]);
+            if (tf32) { x = tf32_round(x); y = tf32_round(y); }
+            acc += x * y;
+        }
+        double v = alpha * acc;
+        if (use_c) v += beta * loadf(c, (nd == 3 ? bb * sc[0] : 0) + m * sc[nd - 2] + n * sc[nd - 1]);
+        vals[s] = v;
+    }
+    (void)shape;
+    return 0;
+}

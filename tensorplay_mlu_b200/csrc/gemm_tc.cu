@@ -1,0 +1,640 @@
+// Tensor-core matrix product for sm_100a: tcgen05.mma with TMEM accumulators,
+// operands staged by TMA into 128-byte-swizzled shared memory, and a
+// persistent, warp-specialised CTA per SM (tensorplay-mlu runs these
+// products on cnnlMatMul_v2 / cnnlStrideBatchMatMul_v3, BlasKernels.cpp:202-242).
+//
+// CTA layout (192 threads, one CTA per SM):
+//   warp 0      TMA producer: one elected thread fills a ring of kStages
+//               shared-memory stages (A: 128 x 64 bf16, B: BN x 64 bf16) and
+//               arms each stage's "full" mbarrier with the byte count;
+//   warp 1      MMA issuer: allocates TMEM (2 accumulators of 128 x BN fp32),
+//               one elected thread issues 4 x tcgen05.mma (K = 16 each) per
+//               stage and releases the stage with tcgen05.commit on its
+//               "empty" mbarrier; after a tile's last stage it commits to the
+//               accumulator's "full" barrier;
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time from the lane
+//               quadrant the warp may access, apply alpha/beta/addend,
+//               convert and store; then release the accumulator.
+// Two accumulators let the epilogue of tile i overlap the mainloop of
+// tile i+1.  Tiles are visited in groups of kGroupM row-tiles so the CTAs in
+// flight share A and B panels in L2.
+//
+// Transposed operands are read in place: an operand whose unit stride is on
+// the M (or N) side is loaded as 64-element MN-major chunks and described to
+// the MMA as MN-major (the instruction descriptor's transpose bits), the way
+// as_operand (BlasKernels.cpp:40-54) passes a transpose flag.
+//
+// Every wait is bounded (kWaitNs): a role that gives up records an error
+// code in the library's device error word, tells the other roles through
+// shared memory, drains what it has in flight and leaves; the host reports
+// it through tp_b200_take_device_error.  No TMA multicast is used.
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "common.h"
+#include "device.cuh"
+#include "gemm.h"
+
+namespace tpb {
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kBM = 128;
+constexpr int kGroupM = 16;
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
+
+// Error codes written to the device error word (role that gave up).
+constexpr int kErrProducer = 0x7c01;
+constexpr int kErrMma = 0x7c02;
+constexpr int kErrEpilogue = 0x7c03;
+
+// ------------------------------------------------------- PTX wrappers --
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wait for the phase of parity `parity` to complete.  False when it did not
+// within kWaitNs, or when another role has already given up.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t start = global_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (global_ns() - start > kWaitNs) {
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+
+template <bool TF32>
+__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                     uint32_t accumulate) {
+    if constexpr (TF32) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    }
+}
+
+// Arrive on `bar` once every tcgen05.mma this thread issued so far is done.
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns of TMEM into 32 registers.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (sm_100 format: start
+// address, leading / stride byte offsets in 16-byte units, version 1 at bit
+// 46, layout type 2 = SWIZZLE_128B at bits 61-63).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((addr >> 4) & 0x3FFF);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32;
+    d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(2) << 61;
+    return d;
+}
+
+// ------------------------------------------------------------ kernel --
+
+struct TcParams {
+    int M, N, K, batch;
+    int m_tiles, n_tiles, k_blocks, num_tiles;
+    int a_mn, b_mn;   // operand stored MN-major (unit stride on M / N)
+    int batched;      // 3-D tensor maps
+    uint32_t idesc;
+    void* c;
+    int64_t sc_b, sc_m;
+    const void* cin;
+    int64_t sci_b, sci_m, sci_n;
+    float alpha, beta;
+    int vec_store;    // 16-byte stores allowed
+    int* err;
+};
+
+// Element traits: 128 bytes of K per stage row in every case.
+template <typename T> struct TcElem;
+template <> struct TcElem<__nv_bfloat16> {
+    static constexpr int kES = 2;
+    static constexpr bool kTF32 = false;
+};
+template <> struct TcElem<__half> {
+    static constexpr int kES = 2;
+    static constexpr bool kTF32 = false;
+};
+template <> struct TcElem<float> {
+    static constexpr int kES = 4;
+    static constexpr bool kTF32 = true;
+};
+
+template <int BN> struct TcShape {
+    static constexpr int kStages = BN == 256 ? 4 : 6;
+    static constexpr int kTmemCols = 2 * BN;  // two accumulators (power of two)
+};
+
+template <typename T, int BN>
+constexpr size_t tc_smem_bytes() {
+    return size_t(TcShape<BN>::kStages) * (kBM * 128 + BN * 128) + 1024 + 256;
+}
+
+__device__ __forceinline__ void tile_coords(const TcParams& p, int tile, int& b, int& mt, int& nt) {
+    const int per_batch = p.m_tiles * p.n_tiles;
+    b = tile / per_batch;
+    const int r = tile - b * per_batch;
+    const int group = kGroupM * p.n_tiles;
+    const int g = r / group;
+    const int first_m = g * kGroupM;
+    const int gsize = min(p.m_tiles - first_m, kGroupM);
+    const int q = r - g * group;
+    mt = first_m + q % gsize;
+    nt = q / gsize;
+}
+
+template <typename T, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const TcParams p) {
+    using E = TcElem<T>;
+    constexpr int kStages = TcShape<BN>::kStages;
+    constexpr int kTmemCols = TcShape<BN>::kTmemCols;
+    constexpr int kEPR = 128 / E::kES;             // elements per 128-byte row (K per stage)
+    constexpr int kUmmaK = 32 / E::kES;            // K per instruction
+    constexpr int kKSteps = kEPR / kUmmaK;         // instructions per stage (4)
+    constexpr uint32_t kABytes = kBM * 128;        // A stage bytes
+    constexpr uint32_t kBBytes = BN * 128;         // B stage bytes
+    constexpr uint32_t kChunk = kEPR * 128;        // one MN-major chunk: kEPR rows of K x 128 B
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem_a = smem;
+    uint8_t* smem_b = smem + kStages * kABytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_b + kStages * kBBytes);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + kStages;
+    uint64_t* acc_full = bars + 2 * kStages;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* drain = acc_empty + 2;
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(smem_addr(&full[s]), 1);
+            mbar_init(smem_addr(&empty[s]), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(smem_addr(&acc_full[a]), 1);
+            mbar_init(smem_addr(&acc_empty[a]), 4);
+        }
+        mbar_init(smem_addr(drain), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_addr(const_cast<uint32_t*>(tmem_slot)), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------------------------------------------- producer --
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+                int b, mt, nt;
+                tile_coords(p, tile, b, mt, nt);
+                const int m0 = mt * kBM, n0 = nt * BN;
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait(smem_addr(&empty[stage]), phase ^ 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t fb = smem_addr(&full[stage]);
+                    mbar_expect_tx(fb, kABytes + kBBytes);
+                    const uint32_t da = smem_addr(smem_a + stage * kABytes);
+                    const uint32_t db = smem_addr(smem_b + stage * kBBytes);
+                    const int k0 = kb * kEPR;
+                    if (p.a_mn) {
+                        for (int j = 0; j < kBM / kEPR; ++j) {
+                            if (p.batched) tma_load_3d(da + j * kChunk, &tmA, fb, m0 + j * kEPR, k0, b);
+                            else tma_load_2d(da + j * kChunk, &tmA, fb, m0 + j * kEPR, k0);
+                        }
+                    } else {
+                        if (p.batched) tma_load_3d(da, &tmA, fb, k0, m0, b);
+                        else tma_load_2d(da, &tmA, fb, k0, m0);
+                    }
+                    if (p.b_mn) {
+                        for (int j = 0; j < BN / kEPR; ++j) {
+                            if (p.batched) tma_load_3d(db + j * kChunk, &tmB, fb, n0 + j * kEPR, k0, b);
+                            else tma_load_2d(db + j * kChunk, &tmB, fb, n0 + j * kEPR, k0);
+                        }
+                    } else {
+                        if (p.batched) tma_load_3d(db, &tmB, fb, k0, n0, b);
+                        else tma_load_2d(db, &tmB, fb, k0, n0);
+                    }
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            if (!ok) {
+                atomicExch(p.err, kErrProducer);
+                // Let the loads already issued land before the CTA leaves:
+                // every stage's most recent phase completes once its bytes do.
+                for (int s = 0; s < kStages; ++s) {
+                    const uint64_t start = global_ns();
+                    while (!mbar_try_wait(smem_addr(&full[s]), (s < stage) ? phase : phase ^ 1)) {
+                        if (global_ns() - start > kWaitNs) break;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------- MMA issuer --
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            bool ok = true;
+            const uint32_t a_lbo = p.a_mn ? kChunk : 16;
+            const uint32_t b_lbo = p.b_mn ? kChunk : 16;
+            const uint32_t a_kstep = p.a_mn ? kUmmaK * 128 : 32;
+            const uint32_t b_kstep = p.b_mn ? kUmmaK * 128 : 32;
+            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++local) {
+                const int acc = local & 1;
+                const uint32_t acc_phase = (local >> 1) & 1;
+                if (!mbar_wait(smem_addr(&acc_empty[acc]), acc_phase ^ 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait(smem_addr(&full[stage]), phase, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_addr(smem_a + stage * kABytes);
+                    const uint32_t sb = smem_addr(smem_b + stage * kBBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kKSteps; ++kk) {
+                        const uint64_t ad = sw128_desc(sa + kk * a_kstep, a_lbo, 1024);
+                        const uint64_t bd = sw128_desc(sb + kk * b_kstep, b_lbo, 1024);
+                        umma<E::kTF32>(d_tmem, ad, bd, p.idesc, (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    umma_commit(smem_addr(&empty[stage]));
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(smem_addr(&acc_full[acc]));
+            }
+            if (!ok) atomicExch(p.err, kErrMma);
+            // Drain: every MMA issued by this thread completes before TMEM
+            // is released.
+            umma_commit(smem_addr(drain));
+            const uint64_t start = global_ns();
+            while (!mbar_try_wait(smem_addr(drain), 0)) {
+                if (global_ns() - start > kWaitNs) break;
+            }
+        }
+    } else {
+        // --------------------------------------------------- epilogue --
+        const int quad = warp & 3;              // TMEM lane quadrant this warp may access
+        const int row_in_tile = quad * 32 + lane;
+        int local = 0;
+        T* c = static_cast<T*>(p.c);
+        const T* cin = static_cast<const T*>(p.cin);
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
+            const int acc = local & 1;
+            const uint32_t acc_phase = (local >> 1) & 1;
+            if (!mbar_wait(smem_addr(&acc_full[acc]), acc_phase, abort_flag)) {
+                if (lane == 0) atomicExch(p.err, kErrEpilogue);
+                break;
+            }
+            tc_fence_after();
+            int b, mt, nt;
+            tile_coords(p, tile, b, mt, nt);
+            const int64_t gm = int64_t(mt) * kBM + row_in_tile;
+            const bool row_ok = gm < p.M;
+            T* crow = c + b * p.sc_b + gm * p.sc_m;
+            const uint32_t t_base = tmem_base + (uint32_t(quad * 32) << 16) + acc * BN;
+#pragma unroll 1
+            for (int chunk = 0; chunk < BN / 32; ++chunk) {
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld32(t_base + chunk * 32, r);
+                tmem_wait_ld();
+                const int64_t n_base = int64_t(nt) * BN + chunk * 32;
+                if (row_ok && n_base < p.N) {
+                    float v[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
+                    if (cin != nullptr) {
+                        const T* crow_in = cin + b * p.sci_b + gm * p.sci_m;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (n_base + j < p.N) v[j] += p.beta * load_as<float>(crow_in[(n_base + j) * p.sci_n]);
+                        }
+                    }
+                    if (p.vec_store && n_base + 32 <= p.N) {
+                        constexpr int V = 16 / sizeof(T);
+#pragma unroll
+                        for (int j = 0; j < 32; j += V) {
+                            Vec<T, V> o;
+#pragma unroll
+                            for (int q = 0; q < V; ++q) o.v[q] = store_as<T>(v[j + q]);
+                            *reinterpret_cast<Vec<T, V>*>(crow + n_base + j) = o;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (n_base + j < p.N) crow[n_base + j] = store_as<T>(v[j]);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_addr(&acc_empty[acc]));
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------ host side --
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        TPB_CUDA(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                                  cudaEnableDefault, &q));
+        TPB_CHECK(q == cudaDriverEntryPointSuccess && ptr != nullptr,
+                  "cuTensorMapEncodeTiled is unavailable from the driver");
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }();
+    return fn;
+}
+
+// Tensor map over an operand seen as [batch][outer][inner] with unit stride
+// on `inner`; box = kEPR x box_outer elements, 128-byte swizzle.
+CUtensorMap make_map(const void* base, CUtensorMapDataType type, int es, int64_t inner, int64_t outer,
+                     int64_t outer_stride, int64_t batch, int64_t batch_stride, uint32_t box_outer) {
+    CUtensorMap map;
+    const int rank = batch > 1 ? 3 : 2;
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
+                          static_cast<cuuint64_t>(batch)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(outer_stride * es),
+                             static_cast<cuuint64_t>(batch_stride * es)};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / es), box_outer, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = encode_fn()(&map, type, rank, const_cast<void*>(base), dims, strides, box, estr,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    TPB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return map;
+}
+
+bool tma_ok(const void* p, int es, int64_t other_stride, int64_t batch, int64_t batch_stride) {
+    if (!aligned16(p)) return false;
+    if (other_stride <= 0 || (other_stride * es) % 16 != 0) return false;
+    if (batch > 1 && (batch_stride <= 0 || (batch_stride * es) % 16 != 0)) return false;
+    return true;
+}
+
+// Per-shape tile choice, computed once and cached (BlasKernels.cpp:70-104
+// caches a CNNL plan per problem the same way).
+int choose_bn(int64_t M, int64_t N, int64_t batch, int sms) {
+    using Key = std::tuple<int64_t, int64_t, int64_t, int>;
+    static std::mutex lock;
+    static std::map<Key, int> cache;
+    const Key key{M, N, batch, sms};
+    {
+        std::lock_guard<std::mutex> g(lock);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    // Cost in units of one 128 x 128 tile; a 128 x 256 tile costs a little
+    // under two (better operand reuse per MMA).
+    auto cost = [&](int bn) {
+        const int64_t tiles = batch * ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
+        const int64_t waves = (tiles + sms - 1) / sms;
+        return static_cast<double>(waves) * (bn == 256 ? 1.9 : 1.0);
+    };
+    const int bn = N <= 128 ? 128 : (cost(256) <= cost(128) ? 256 : 128);
+    std::lock_guard<std::mutex> g(lock);
+    cache[key] = bn;
+    return bn;
+}
+
+template <typename T, int BN>
+void launch_tc(const GemmProblem& p, const CUtensorMap& ma, const CUtensorMap& mb, TcParams& tp,
+               int dev, cudaStream_t stream) {
+    constexpr size_t smem = tc_smem_bytes<T, BN>();
+    static bool configured[64] = {};
+    if (!configured[dev]) {
+        TPB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(smem)));
+        configured[dev] = true;
+    }
+    tp.m_tiles = static_cast<int>((p.M + kBM - 1) / kBM);
+    tp.n_tiles = static_cast<int>((p.N + BN - 1) / BN);
+    tp.num_tiles = static_cast<int>(p.batch) * tp.m_tiles * tp.n_tiles;
+    // Instruction descriptor: fp32 accumulate (bit 4), A/B format (bits 7-9,
+    // 10-12: f16 0, bf16 1, tf32 2), A/B MN-major (bits 15, 16), N >> 3
+    // (bits 17-22), M >> 4 (bits 24-28).
+    const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : std::is_same<T, float>::value ? 2u : 0u;
+    tp.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (uint32_t(tp.a_mn) << 15) |
+               (uint32_t(tp.b_mn) << 16) | (uint32_t(BN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
+    const int grid = std::min(tp.num_tiles, num_sms(dev));
+    gemm_tc_kernel<T, BN><<<grid, kThreads, smem, stream>>>(ma, mb, tp);
+    check_launch("gemm_tc");
+}
+
+template <typename T>
+bool gemm_tc_typed(const GemmProblem& p, int dev, cudaStream_t stream, CUtensorMapDataType type) {
+    constexpr int es = sizeof(T);
+    // A: K-major (unit stride along K) or M-major; same for B along K / N.
+    const bool a_k = p.sa_k == 1 || p.K == 1;
+    const bool a_m = !a_k && (p.sa_m == 1 || p.M == 1);
+    const bool b_k = p.sb_k == 1 || p.K == 1;
+    const bool b_n = !b_k && (p.sb_n == 1 || p.N == 1);
+    if (!(a_k || a_m) || !(b_k || b_n)) return false;
+    if (!tma_ok(p.a, es, a_k ? p.sa_m : p.sa_k, p.batch, p.sa_b)) return false;
+    if (!tma_ok(p.b, es, b_k ? p.sb_n : p.sb_k, p.batch, p.sb_b)) return false;
+    if (p.M >= (int64_t(1) << 31) || p.N >= (int64_t(1) << 31) || p.K >= (int64_t(1) << 31)) return false;
+    const int sms = num_sms(dev);
+    const int bn = choose_bn(p.M, p.N, p.batch, sms);
+    constexpr int kEPR = 128 / es;
+    // A box: K-major 64 x 128 rows; M-major 64 (M) x 64 (K) chunks.
+    const CUtensorMap ma = a_k ? make_map(p.a, type, es, p.K, p.M, p.sa_m, p.batch, p.sa_b, kBM)
+                               : make_map(p.a, type, es, p.M, p.K, p.sa_k, p.batch, p.sa_b, kEPR);
+    const CUtensorMap mb = b_k ? make_map(p.b, type, es, p.K, p.N, p.sb_n, p.batch, p.sb_b, bn)
+                               : make_map(p.b, type, es, p.N, p.K, p.sb_k, p.batch, p.sb_b, kEPR);
+    TcParams tp{};
+    tp.M = static_cast<int>(p.M);
+    tp.N = static_cast<int>(p.N);
+    tp.K = static_cast<int>(p.K);
+    tp.batch = static_cast<int>(p.batch);
+    tp.k_blocks = static_cast<int>((p.K + kEPR - 1) / kEPR);
+    tp.a_mn = a_k ? 0 : 1;
+    tp.b_mn = b_k ? 0 : 1;
+    tp.batched = p.batch > 1 ? 1 : 0;
+    tp.c = p.c;
+    tp.sc_b = p.sc_b;
+    tp.sc_m = p.sc_m;
+    tp.cin = p.cin;
+    tp.sci_b = p.sci_b;
+    tp.sci_m = p.sci_m;
+    tp.sci_n = p.sci_n;
+    tp.alpha = static_cast<float>(p.alpha);
+    tp.beta = static_cast<float>(p.beta);
+    tp.vec_store = aligned16(p.c) && (p.sc_m * es) % 16 == 0 && (p.batch == 1 || (p.sc_b * es) % 16 == 0);
+    tp.err = device_error_word(dev);
+    if (bn == 256) launch_tc<T, 256>(p, ma, mb, tp, dev, stream);
+    else launch_tc<T, 128>(p, ma, mb, tp, dev, stream);
+    return true;
+}
+
+}  // namespace
+
+bool gemm_tc(const GemmProblem& p, int dev, cudaStream_t stream) {
+    if (p.M == 0 || p.N == 0 || p.K == 0) return false;
+    switch (p.dtype) {
+        case TPB_BF16: return gemm_tc_typed<__nv_bfloat16>(p, dev, stream, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+        case TPB_F16: return gemm_tc_typed<__half>(p, dev, stream, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+        case TPB_F32:
+            if (!(p.flags & TPB_GEMM_ALLOW_TF32)) return false;
+            return gemm_tc_typed<float>(p, dev, stream, CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
+        default: return false;
+    }
+}
+
+}  // namespace tpb

@@ -1,0 +1,169 @@
+"""Data-parallel MLP training step on the B200 backend.
+
+The model of tensorplay-mlu's README distributed benchmark, at the sizes the
+B200 build is measured on: Linear(4096 -> 16384), GELU, Linear(16384 -> 4096),
+bf16 weights with PyTorch's nn.Linear initialisation (Kaiming-uniform, bound
+1/sqrt(fan_in)) from seed 0, loss = mean((out - target)^2), full backward
+(no input gradient) and an SGD update.  Every step is a sequence of the
+backend's own operators -- the ones TensorPlay's autograd engine would call
+for this model (linear, gelu, sub, pow, mean, mul, mm on transposed views,
+sum over dim 0, gelu_backward, add_) -- so the step exercises the claimed
+kernels end to end.
+
+Data parallelism (one rank per GPU): gradients live in one flat buffer split
+into two buckets in backward order, (dW2, db2) then (dW1, db1).  Each bucket
+is all-reduced (SUM) on a side stream as soon as backward has produced it,
+so the first exchange overlaps the dh / dW1 GEMMs; the AVG's 1/world scale is
+folded into the SGD step (p -= lr/world * g_sum), not launched as its own
+pass as tensorplay_mlu/distributed.py:241-242 does.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _native as N
+from . import ops
+
+
+@dataclass
+class MLPConfig:
+    d_in: int = 4096
+    d_hidden: int = 16384
+    batch: int = 8192
+    lr: float = 1e-3
+    dtype: torch.dtype = torch.bfloat16
+
+
+def init_params_host(cfg: MLPConfig, seed: int = 0):
+    """Host weights, nn.Linear's default init: U(-1/sqrt(fan_in), 1/sqrt(fan_in))."""
+    g = torch.Generator().manual_seed(seed)
+
+    def uniform(shape, fan_in):
+        bound = 1.0 / math.sqrt(fan_in)
+        return (torch.rand(shape, generator=g, dtype=torch.float32) * 2 - 1) * bound
+
+    w1 = uniform((cfg.d_hidden, cfg.d_in), cfg.d_in).to(cfg.dtype)
+    b1 = uniform((cfg.d_hidden,), cfg.d_in).to(cfg.dtype)
+    w2 = uniform((cfg.d_in, cfg.d_hidden), cfg.d_hidden).to(cfg.dtype)
+    b2 = uniform((cfg.d_in,), cfg.d_hidden).to(cfg.dtype)
+    return w1, b1, w2, b2
+
+
+def make_batch_host(cfg: MLPConfig, seed: int):
+    """Synthetic input and target, ~N(0, 1), from ``seed`` (the rank)."""
+    g = torch.Generator().manual_seed(1000 + seed)
+    x = torch.randn((cfg.batch, cfg.d_in), generator=g, dtype=torch.float32).to(cfg.dtype)
+    t = torch.randn((cfg.batch, cfg.d_in), generator=g, dtype=torch.float32).to(cfg.dtype)
+    return x, t
+
+
+class DataParallelMLP:
+    """Parameters, gradient buckets and the training step of one rank."""
+
+    def __init__(self, cfg: MLPConfig, device: int = 0, pg=None, host_params=None):
+        self.cfg = cfg
+        self.device = torch.device("cuda", device)
+        self.pg = pg
+        self.world = pg.size() if pg is not None else 1
+        w1, b1, w2, b2 = host_params if host_params is not None else init_params_host(cfg)
+        dev = self.device
+        # Parameters.
+        self.w1 = ops.to_device(w1, dev)
+        self.b1 = ops.to_device(b1, dev)
+        self.w2 = ops.to_device(w2, dev)
+        self.b2 = ops.to_device(b2, dev)
+        # One flat gradient buffer, bucket A = (dW2, db2), bucket B = (dW1, db1).
+        H, D = cfg.d_hidden, cfg.d_in
+        n_a = D * H + D
+        n_b = H * D + H
+        self.grad_flat = torch.empty(n_a + n_b, dtype=cfg.dtype, device=dev)
+        self.bucket_a = self.grad_flat.narrow(0, 0, n_a)
+        self.bucket_b = self.grad_flat.narrow(0, n_a, n_b)
+        self.dw2 = self.bucket_a.narrow(0, 0, D * H).view(D, H)
+        self.db2 = self.bucket_a.narrow(0, D * H, D)
+        self.dw1 = self.bucket_b.narrow(0, 0, H * D).view(H, D)
+        self.db1 = self.bucket_b.narrow(0, H * D, H)
+        self.comm_stream = torch.cuda.Stream(device=dev) if pg is not None and self.world > 1 else None
+        # When a list, every GEMM of the step appends a (start, end) pair of
+        # CUDA events recorded around its launch on the current stream.
+        self.gemm_events: Optional[list] = None
+
+    def _timed(self, fn, *args):
+        if self.gemm_events is None:
+            return fn(*args)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        out = fn(*args)
+        end.record()
+        self.gemm_events.append((start, end))
+        return out
+
+    def params(self):
+        return [self.w1, self.b1, self.w2, self.b2]
+
+    def grads(self):
+        return [self.dw1, self.db1, self.dw2, self.db2]
+
+    # -- kernels with preallocated outputs ----------------------------------
+    @staticmethod
+    def _mm_into(out, a, b):
+        return ops._gemm(out, a, b)
+
+    @staticmethod
+    def _colsum_into(out, x):
+        """sum(x, dim=0) written into ``out`` (the bias gradient)."""
+        N.check(N.lib().tp_b200_reduce(N.SUM, N.describe(out.view(1, -1)), N.describe(x), 1,
+                                       N.stream_of(x.device)), "sum")
+        return out
+
+    def _allreduce_async(self, bucket, ready_event):
+        """SUM all-reduce of ``bucket`` on the comm stream after ``ready_event``."""
+        self.comm_stream.wait_event(ready_event)
+        with torch.cuda.stream(self.comm_stream):
+            work = self.pg.allreduce([bucket], op=0)
+        return work
+
+    def step(self, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
+        """One forward + backward + SGD step; returns the loss (device 0-d tensor)."""
+        cfg = self.cfg
+        # forward
+        h = self._timed(ops.linear, x, self.w1, self.b1)
+        a = ops.gelu(h)
+        out = self._timed(ops.linear, a, self.w2, self.b2)
+        diff = ops.sub_Tensor(out, target)
+        loss = ops.mean(ops.pow_Tensor_Scalar(diff, 2))
+        # backward of mean((out - t)^2): d out = 2 (out - t) / numel
+        d_out = ops.mul_Scalar(diff, 2.0 / diff.numel())
+        self._timed(self._mm_into, self.dw2, d_out.t(), a)
+        self._colsum_into(self.db2, d_out)
+        work_a = None
+        if self.comm_stream is not None:
+            ev = torch.cuda.Event()
+            ev.record()
+            work_a = self._allreduce_async(self.bucket_a, ev)
+        d_a = self._timed(ops.mm, d_out, self.w2)
+        d_h = ops.gelu_backward(d_a, h)
+        self._timed(self._mm_into, self.dw1, d_h.t(), x)
+        self._colsum_into(self.db1, d_h)
+        scale = -cfg.lr
+        if self.comm_stream is not None:
+            ev = torch.cuda.Event()
+            ev.record()
+            work_b = self._allreduce_async(self.bucket_b, ev)
+            work_a.wait()
+            work_b.wait()
+            scale = -cfg.lr / self.world
+        # SGD: p += (-lr / world) * g_sum
+        for p, g in zip(self.params(), self.grads()):
+            ops.add__Tensor(p, g, alpha=scale)
+        return loss
+
+    def flops_per_step(self) -> float:
+        """Five GEMMs of 2 * B * D * H each (forward 2, backward 3, no dX)."""
+        c = self.cfg
+        return 5 * 2.0 * c.batch * c.d_in * c.d_hidden

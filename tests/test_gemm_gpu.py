@@ -1,0 +1,197 @@
+"""Matrix products on a B200 against the oracle (tensorplay-mlu
+tests/test_mlu.py:238-300 structure): transposes read in place, addmm / bmm /
+matmul / linear, the reference's shape list, the TF32 switch, and the
+BASELINE GEMM shapes checked on sampled outputs.  bf16/f16 products run on
+the tcgen05 kernel, exact fp32 / f64 / integer on the CUDA-core kernel."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from conftest import TOL, assert_close, assert_equal
+
+pytestmark = pytest.mark.gpu
+
+FLOATS = [torch.float32, torch.bfloat16, torch.float16]
+
+
+def rand(*shape, dtype=torch.float32, seed=0, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * scale).to(dtype)
+
+
+@pytest.fixture(scope="module")
+def ops(backend):
+    return backend.ops
+
+
+def dev(ops, t):
+    return ops.to_device(t)
+
+
+def check_sampled(got_dev, a, b, c=None, alpha=1.0, beta=0.0, flags=0, samples=2048, seed=0):
+    """Compare `samples` random outputs of a large product with the oracle
+    (float64 accumulation), relative to the largest |reference| sampled."""
+    got = got_dev.cpu() if got_dev.device.type != "cpu" else got_dev
+    rng = np.random.default_rng(seed)
+    if got.dim() == 2:
+        idx = np.stack([np.zeros(samples, np.int64), rng.integers(0, got.shape[0], samples),
+                        rng.integers(0, got.shape[1], samples)], 1)
+        vals = got[idx[:, 1], idx[:, 2]]
+    else:
+        idx = np.stack([rng.integers(0, got.shape[0], samples), rng.integers(0, got.shape[1], samples),
+                        rng.integers(0, got.shape[2], samples)], 1)
+        vals = got[idx[:, 0], idx[:, 1], idx[:, 2]]
+    want = O.gemm_sampled(a, b, idx, c, alpha, beta, flags)
+    err = np.abs(vals.double().numpy() - want).max()
+    ref = max(np.abs(want).max(), 1.0)
+    return err / ref
+
+
+@pytest.mark.parametrize("dtype", FLOATS + [torch.float64])
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True), (True, True)])
+def test_mm_transposes(ops, dtype, ta, tb):
+    a, b = rand(37, 19, dtype=dtype), rand(19, 23, dtype=dtype, seed=3)
+    da = dev(ops, a.t().contiguous()).t() if ta else dev(ops, a)
+    db = dev(ops, b.t().contiguous()).t() if tb else dev(ops, b)
+    assert_close(ops.mm(da, db), O.gemm(a, b), dtype, scale=5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True), (True, True)])
+def test_tensor_core_transposes(ops, dtype, ta, tb):
+    # Aligned shapes so every transpose combination takes the tcgen05 path
+    # (K-major and MN-major shared-memory operands), with M, N, K tails.
+    M, N, K = 200, 328, 136
+    a, b = rand(M, K, dtype=dtype, seed=1), rand(K, N, dtype=dtype, seed=2)
+    da = dev(ops, a.t().contiguous()).t() if ta else dev(ops, a)
+    db = dev(ops, b.t().contiguous()).t() if tb else dev(ops, b)
+    assert_close(ops.mm(da, db), O.gemm(a, b), dtype, scale=K ** 0.5)
+
+
+@pytest.mark.parametrize("dtype", [torch.int32, torch.int64, torch.int8])
+def test_integer_mm_is_exact(ops, dtype):
+    g = torch.Generator().manual_seed(0)
+    a = torch.randint(-9, 9, (37, 19), generator=g).to(dtype)
+    b = torch.randint(-9, 9, (19, 23), generator=g).to(dtype)
+    assert_equal(ops.mm(dev(ops, a), dev(ops, b)).cpu(), O.gemm(a, b))
+
+
+@pytest.mark.parametrize("dtype", FLOATS)
+def test_addmm_bmm_matmul(ops, dtype):
+    bias, a, b = rand(23, dtype=dtype), rand(37, 19, dtype=dtype, seed=1), rand(19, 23, dtype=dtype, seed=2)
+    assert_close(ops.addmm(dev(ops, bias), dev(ops, a), dev(ops, b), beta=0.5, alpha=2.0),
+                 O.gemm(a, b, bias, 2.0, 0.5), dtype, scale=10)
+    x, y = rand(4, 9, 6, dtype=dtype), rand(4, 6, 5, dtype=dtype, seed=4)
+    assert_close(ops.bmm(dev(ops, x), dev(ops, y)), O.gemm(x, y), dtype, scale=5)
+    w = rand(6, 5, dtype=dtype, seed=5)
+    assert_close(ops.matmul(dev(ops, x), dev(ops, w)),
+                 O.gemm(x.reshape(-1, 6), w).reshape(4, 9, 5), dtype, scale=5)
+    v = rand(2, 1, 6, 3, dtype=dtype, seed=6)
+    want = O.gemm(x.unsqueeze(0).expand(2, 4, 9, 6).reshape(8, 9, 6).contiguous(),
+                  v.expand(2, 4, 6, 3).reshape(8, 6, 3).contiguous()).reshape(2, 4, 9, 3)
+    assert_close(ops.matmul(dev(ops, x), dev(ops, v)), want, dtype, scale=5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_addmm_bias_in_epilogue_on_tensor_cores(ops, dtype):
+    M, N, K = 256, 384, 128
+    bias, a, b = rand(N, dtype=dtype), rand(M, K, dtype=dtype, seed=1), rand(K, N, dtype=dtype, seed=2)
+    assert_close(ops.addmm(dev(ops, bias), dev(ops, a), dev(ops, b)), O.gemm(a, b, bias, 1.0, 1.0),
+                 dtype, scale=K ** 0.5)
+    full = rand(M, N, dtype=dtype, seed=3)
+    assert_close(ops.addmm(dev(ops, full), dev(ops, a), dev(ops, b), beta=0.25, alpha=-1.0),
+                 O.gemm(a, b, full, -1.0, 0.25), dtype, scale=K ** 0.5)
+
+
+@pytest.mark.parametrize("dtype", FLOATS)
+@pytest.mark.parametrize("m,k,n", [(2, 1024, 1024), (128, 1024, 256), (256, 4096, 1024),
+                                   (1024, 4096, 128), (4096, 4096, 4096)])
+def test_mm_shapes(ops, dtype, m, k, n):
+    a, b = rand(m, k, dtype=dtype, seed=1), rand(k, n, dtype=dtype, seed=2)
+    got = ops.mm(dev(ops, a), dev(ops, b))
+    rel = check_sampled(got, a, b)
+    assert rel <= TOL[dtype] * k ** 0.5, rel
+
+
+@pytest.mark.parametrize("dtype", FLOATS)
+def test_linear(ops, dtype):
+    x, w, b = rand(3, 5, 64, dtype=dtype), rand(48, 64, dtype=dtype, seed=1), rand(48, dtype=dtype, seed=2)
+    xd, wd, bd = dev(ops, x), dev(ops, w), dev(ops, b)
+    want = O.gemm(x.reshape(15, 64), w.t()).reshape(3, 5, 48)
+    want_b = O.gemm(x.reshape(15, 64), w.t(), b, 1.0, 1.0).reshape(3, 5, 48)
+    assert_close(ops.linear(xd, wd, bd), want_b, dtype, scale=8)
+    assert_close(ops.linear(xd, wd), want, dtype, scale=8)
+    assert_close(ops.linear(xd[0, 0], wd, bd), want_b[0, 0], dtype, scale=8)
+
+
+@pytest.mark.parametrize("dtype", FLOATS)
+def test_bmm_shapes(ops, dtype):
+    for (bt, m, k, n) in ((32, 512, 64, 512), (1, 256, 4096, 1024), (3, 1, 7, 5)):
+        a, b = rand(bt, m, k, dtype=dtype, seed=1), rand(bt, k, n, dtype=dtype, seed=2)
+        got = ops.bmm(dev(ops, a), dev(ops, b))
+        assert check_sampled(got, a, b) <= TOL[dtype] * k ** 0.5
+    a, b = rand(4, 9, 6, dtype=dtype), rand(4, 5, 6, dtype=dtype, seed=3)
+    assert_close(ops.bmm(dev(ops, a), dev(ops, b).transpose(1, 2)), O.gemm(a, b.transpose(1, 2)),
+                 dtype, scale=5)
+
+
+def test_float32_matmul_precision_selects_tf32(ops):
+    a, b = rand(512, 512, seed=1), rand(512, 512, seed=2)
+    want = O.gemm(a.double(), b.double())
+    da, db = dev(ops, a), dev(ops, b)
+    previous = torch.get_float32_matmul_precision()
+    torch.set_float32_matmul_precision("highest")
+    try:
+        exact = (ops.mm(da, db).cpu().double() - want).abs().max().item()
+        torch.set_float32_matmul_precision("high")
+        fast = (ops.mm(da, db).cpu().double() - want).abs().max().item()
+    finally:
+        torch.set_float32_matmul_precision(previous)
+    assert exact < 1e-3, exact
+    assert fast < 0.5, fast  # TF32 keeps 10 mantissa bits
+    assert fast > exact  # the switch really selected another path
+
+
+# ------------------------------------------------- BASELINE GEMM shapes --
+
+def test_baseline_mm_8192_bf16(ops):
+    n = 8192
+    a, b = rand(n, n, dtype=torch.bfloat16, seed=1, scale=n ** -0.5), rand(n, n, dtype=torch.bfloat16, seed=2)
+    got = ops.mm(dev(ops, a), dev(ops, b))
+    assert check_sampled(got, a, b) <= 1e-2
+
+
+def test_baseline_addmm_and_linear_bf16(ops):
+    M, K, N = 16384, 4096, 11008
+    a = rand(M, K, dtype=torch.bfloat16, seed=1)
+    w = rand(N, K, dtype=torch.bfloat16, seed=2, scale=K ** -0.5)
+    bias = rand(N, dtype=torch.bfloat16, seed=3)
+    da, dw, db = dev(ops, a), dev(ops, w), dev(ops, bias)
+    lin = ops.linear(da, dw, db)          # weight [N, K] read transposed in place
+    assert check_sampled(lin, a, w.t(), bias, 1.0, 1.0) <= 1e-2
+    b = w.t().contiguous()
+    add = ops.addmm(db, da, dev(ops, b))  # [K, N] row-major
+    assert check_sampled(add, a, b, bias, 1.0, 1.0) <= 1e-2
+
+
+def test_baseline_bmm_bf16(ops):
+    a = rand(64, 2048, 128, dtype=torch.bfloat16, seed=1, scale=128 ** -0.5)
+    b = rand(64, 128, 2048, dtype=torch.bfloat16, seed=2)
+    got = ops.bmm(dev(ops, a), dev(ops, b))
+    assert check_sampled(got, a, b) <= 1e-2
+
+
+def test_baseline_mm_4096_fp32_highest(ops):
+    n = 4096
+    a, b = rand(n, n, seed=1, scale=n ** -0.5), rand(n, n, seed=2)
+    previous = torch.get_float32_matmul_precision()
+    torch.set_float32_matmul_precision("highest")
+    try:
+        got = ops.mm(dev(ops, a), dev(ops, b))
+    finally:
+        torch.set_float32_matmul_precision(previous)
+    assert check_sampled(got, a, b) <= 1e-5

@@ -1,0 +1,63 @@
+"""Host-side operator logic without a GPU: dtype promotion, result shapes and
+argument checks mirror the host framework's (PyTorch CPU stands in for
+TensorPlay's), and the collective helpers' split arithmetic."""
+
+from __future__ import annotations
+
+import itertools
+
+import pytest
+import torch
+
+from tensorplay_mlu_b200 import distributed as D
+from tensorplay_mlu_b200 import ops
+
+DTYPES = [torch.uint8, torch.int8, torch.int16, torch.int32, torch.int64, torch.float16,
+          torch.bfloat16, torch.float32, torch.float64, torch.bool]
+
+
+@pytest.mark.parametrize("da,db", list(itertools.product(DTYPES, DTYPES)))
+def test_binary_promotion_matches_host(da, db):
+    a = torch.zeros(3, 2, dtype=da)
+    b = torch.zeros(2, dtype=db)
+    assert ops.binary_result_dtype(a, b) == torch.result_type(a, b)
+    s = torch.zeros((), dtype=db)
+    assert ops.binary_result_dtype(a, s) == torch.result_type(a, s)
+
+
+@pytest.mark.parametrize("dt", DTYPES)
+@pytest.mark.parametrize("value", [2, 2.5, True])
+def test_scalar_promotion_matches_host(dt, value):
+    a = torch.zeros(3, dtype=dt)
+    assert ops.scalar_result_dtype(dt, value) == torch.result_type(a, value)
+
+
+def test_dims_normalisation():
+    t = torch.zeros(2, 3, 4)
+    assert ops._dims(t, -1) == [2]
+    assert ops._dims(t, [0, -1]) == [0, 2]
+    assert ops._dims(t, None) == [0, 1, 2]
+    with pytest.raises(IndexError):
+        ops._dims(t, 3)
+    with pytest.raises(RuntimeError):
+        ops._dims(t, [1, -2])
+
+
+def test_device_operators_reject_host_tensors():
+    with pytest.raises(RuntimeError):
+        ops.exp(torch.zeros(3))
+    with pytest.raises(RuntimeError):
+        ops.mm(torch.zeros(2, 2), torch.zeros(2, 2))
+
+
+def test_all_to_all_split_arithmetic():
+    t = torch.zeros(6, 4)
+    assert D._element_counts(t, [1, 2, 3], 3) == [4, 8, 12]
+    assert D._element_counts(t, None, 2) == [12, 12]
+    assert D._prefix_offsets([4, 8, 12]) == [0, 4, 12]
+
+
+def test_reduction_table_matches_the_reference():
+    # AVG is SUM plus a 1/world scale (tensorplay_mlu/distributed.py:48-58).
+    assert D._REDUCTIONS[D.ReduceOp.AVG] == (0, None)
+    assert D._REDUCTIONS[D.ReduceOp.MAX][0] == 2 and D._REDUCTIONS[D.ReduceOp.MIN][0] == 3
