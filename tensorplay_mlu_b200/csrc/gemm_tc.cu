@@ -35,6 +35,7 @@
 #include <cudaTypedefs.h>
 
 #include <map>
+#include <memory>
 #include <mutex>
 #include <tuple>
 
@@ -43,6 +44,8 @@
 #include "gemm.h"
 
 namespace tpb {
+
+void copy_impl(const tpb_tensor& dst, const tpb_tensor& src, cudaStream_t stream, int dev);
 
 namespace {
 
@@ -579,8 +582,60 @@ void launch_tc(const GemmProblem& p, const CUtensorMap& ma, const CUtensorMap& m
 }
 
 template <typename T>
-bool gemm_tc_typed(const GemmProblem& p, int dev, cudaStream_t stream, CUtensorMapDataType type) {
+bool gemm_tc_typed(const GemmProblem& p_in, int dev, cudaStream_t stream, CUtensorMapDataType type) {
     constexpr int es = sizeof(T);
+    GemmProblem p = p_in;
+    // TF32 operands must be K-major here: the 128-byte-swizzled MN-major
+    // layout this kernel stages is defined for 16-bit elements only (32-bit
+    // MN-major operands need the 32-byte-atom swizzle variant).  An MN-major
+    // fp32 operand is first copied K-major (one transposing pass).
+    std::unique_ptr<Scratch> a_copy, b_copy;
+    if constexpr (std::is_same<T, float>::value) {
+        if (!(p.sa_k == 1 || p.K == 1)) {
+            a_copy.reset(new Scratch(sizeof(float) * p.batch * p.M * p.K, dev, stream));
+            Scratch& tmp = *a_copy;
+            tpb_tensor src{}, dst{};
+            src.data = const_cast<void*>(p.a);
+            src.dtype = dst.dtype = TPB_F32;
+            src.ndim = dst.ndim = 3;
+            const int64_t sizes[3] = {p.batch, p.M, p.K};
+            const int64_t sstr[3] = {p.sa_b, p.sa_m, p.sa_k};
+            const int64_t dstr[3] = {p.M * p.K, p.K, 1};
+            for (int i = 0; i < 3; ++i) {
+                src.sizes[i] = dst.sizes[i] = sizes[i];
+                src.strides[i] = sstr[i];
+                dst.strides[i] = dstr[i];
+            }
+            dst.data = tmp.get();
+            copy_impl(dst, src, stream, dev);
+            p.a = tmp.get();
+            p.sa_b = p.batch > 1 ? p.M * p.K : 0;
+            p.sa_m = p.K;
+            p.sa_k = 1;
+        }
+        if (!(p.sb_k == 1 || p.K == 1)) {
+            b_copy.reset(new Scratch(sizeof(float) * p.batch * p.N * p.K, dev, stream));
+            Scratch& tmp = *b_copy;
+            tpb_tensor src{}, dst{};
+            src.data = const_cast<void*>(p.b);
+            src.dtype = dst.dtype = TPB_F32;
+            src.ndim = dst.ndim = 3;
+            const int64_t sizes[3] = {p.batch, p.N, p.K};
+            const int64_t sstr[3] = {p.sb_b, p.sb_n, p.sb_k};
+            const int64_t dstr[3] = {p.N * p.K, p.K, 1};
+            for (int i = 0; i < 3; ++i) {
+                src.sizes[i] = dst.sizes[i] = sizes[i];
+                src.strides[i] = sstr[i];
+                dst.strides[i] = dstr[i];
+            }
+            dst.data = tmp.get();
+            copy_impl(dst, src, stream, dev);
+            p.b = tmp.get();
+            p.sb_b = p.batch > 1 ? p.N * p.K : 0;
+            p.sb_n = p.K;
+            p.sb_k = 1;
+        }
+    }
     // A: K-major (unit stride along K) or M-major; same for B along K / N.
     const bool a_k = p.sa_k == 1 || p.K == 1;
     const bool a_m = !a_k && (p.sa_m == 1 || p.M == 1);
