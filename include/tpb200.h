@@ -211,6 +211,21 @@ enum tpb_reduce_op { TPB_SUM = 0, TPB_MEAN = 1, TPB_AMAX = 2, TPB_AMIN = 3 };
  * x's (sum of int32 into int64, sum(dtype=...)). */
 int tp_b200_reduce(int op, const tpb_tensor* out, const tpb_tensor* x, uint32_t dim_mask,
                    void* stream);
+/* No counterpart in the reference: tp_b200_reduce for callers that cannot
+ * allocate device memory when they reduce (a process whose GPU memory is
+ * reserved up front by its own pool, or a path that must not risk a
+ * cudaMalloc on an allocator miss).  Same arguments, kernels, split policy
+ * and results as tp_b200_reduce, but it allocates nothing: the per-block
+ * partial results go to one static 8 MiB device array per GPU (held by every
+ * GPU that loads the library until the process exits).  A reduction whose
+ * partial results would exceed 8 MiB, whose input layout would need a
+ * gathered copy, or whose result dtype is neither the input's nor the
+ * accumulator's is rejected with an error (use tp_b200_reduce).  The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress
+ * with that device current); make that first call before any stream capture.
+ * All calls share the array, so calls whose work overlaps on the GPU race. */
+int tp_b200_reduce_noalloc(int op, const tpb_tensor* out, const tpb_tensor* x, uint32_t dim_mask,
+                           void* stream);
 /* ReduceKernels.cpp:146-199 softmax_forward over dimension `dim`
  * (log != 0: log_softmax).  Max-subtracted, single read of the row. */
 int tp_b200_softmax(int log, const tpb_tensor* out, const tpb_tensor* x, int dim, void* stream);

@@ -108,6 +108,7 @@ _SIGNATURES = {
     "tp_b200_unary": ([_I, _T, _T, _D, _P], _I),
     "tp_b200_unary_backward": ([_I, _T, _T, _T, _D, _P], _I),
     "tp_b200_reduce": ([_I, _T, _T, ctypes.c_uint32, _P], _I),
+    "tp_b200_reduce_noalloc": ([_I, _T, _T, ctypes.c_uint32, _P], _I),
     "tp_b200_softmax": ([_I, _T, _T, _I, _P], _I),
     "tp_b200_softmax_backward": ([_I, _T, _T, _T, _I, _P], _I),
     "tp_b200_gemm": ([_T, _T, _T, _T, _D, _D, _I, _P], _I),

@@ -25,6 +25,7 @@
 
 #include <cfloat>
 #include <climits>
+#include <mutex>
 #include <type_traits>
 
 #include "common.h"
@@ -767,7 +768,212 @@ void check_same_shape(const tpb_tensor& a, const tpb_tensor& b, const char* what
 }  // namespace
 }  // namespace tpb
 
+// ---------------------------------------------------------------------------
+// Allocation-free reductions (tp_b200_reduce_noalloc).
+//
+// Some callers cannot allocate device memory at the moment they reduce: a
+// serving process whose GPU memory is reserved up front by its own pool, so a
+// library allocation behind its back can fail or break its accounting; or a
+// latency-critical path that must not risk cudaMalloc (which can synchronise
+// the device) when the caching allocator misses.  For them the reduction's
+// per-block partial results live in this fixed array instead of the caching
+// allocator.  It is 8 MiB per GPU, reserved by every GPU that loads the
+// library until the process exits, and it is shared by every call: a call
+// overwrites what the previous one left (every partial slot a launch reads is
+// written by that launch first, so nothing needs clearing), and two calls
+// whose work overlaps on the GPU race on it.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) unsigned char g_reduce_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace tpb {
+namespace {
+
+std::mutex g_noalloc_lock;
+void* g_noalloc_ptr[64] = {};
+
+// Device address of the array on `dev` (the caller has made `dev` current).
+// In host code the array's name is only a host-side handle, so the address is
+// looked up once per device and cached.
+void* noalloc_scratch(int dev) {
+    TPB_CHECK(dev >= 0 && dev < 64, "invalid device index %d", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_lock);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        TPB_CUDA(cudaGetSymbolAddress(&p, g_reduce_noalloc_scratch));
+        TPB_CHECK(p != nullptr, "reduce_noalloc: no device address for the static scratch");
+        g_noalloc_ptr[dev] = p;
+    }
+    return g_noalloc_ptr[dev];
+}
+
+void check_noalloc_fit(size_t nbytes) {
+    TPB_CHECK(nbytes <= kNoAllocScratchBytes,
+              "reduce_noalloc: this reduction needs %zu bytes of partial results, more than the "
+              "%zu-byte static scratch of the allocation-free entry point; use tp_b200_reduce",
+              nbytes, kNoAllocScratchBytes);
+}
+
+// Same kernels and the same split policy as reduce_launch, with the partial
+// results in the static array; layouts that would need a gathered copy of the
+// input are refused.
+template <typename T, typename To, int OP>
+void reduce_launch_noalloc(const tpb_tensor& out, const tpb_tensor& xin, uint32_t mask, int dev,
+                           cudaStream_t stream, void* scratch) {
+    using A = typename Acc<T>::type;
+    constexpr int V = VecWidth<T>::value;
+    const int sms = num_sms(dev);
+    DimGroup kept, red;
+    for (int i = 0; i < xin.ndim; ++i) {
+        DimGroup& g = (mask >> i) & 1 ? red : kept;
+        g.sizes[g.n] = xin.sizes[i];
+        g.strides[g.n] = xin.strides[i];
+        ++g.n;
+    }
+    const int64_t rows = kept.numel();
+    const int64_t R = red.numel();
+    if (R == 1) {
+        copy_impl(out, xin, stream, dev);
+        return;
+    }
+    kept.coalesce();
+    red.coalesce();
+    To* o = static_cast<To*>(out.data);
+    const double count = static_cast<double>(R);
+    const T* x = static_cast<const T*>(xin.data);
+    A* partial = static_cast<A*>(scratch);
+
+    const bool cols = red.n == 1 && kept.n >= 1 && kept.n <= 2 && kept.strides[kept.n - 1] == 1 &&
+                      red.strides[0] != 1;
+    if (cols) {
+        const int64_t K = kept.sizes[kept.n - 1];
+        const int64_t O = kept.n == 2 ? kept.sizes[0] : 1;
+        const int64_t os = kept.n == 2 ? kept.strides[0] : 0;
+        const int64_t rs = red.strides[0];
+        const bool vec = K % V == 0 && rs % V == 0 && os % V == 0 && aligned16(x);
+        const int vw = vec ? V : 1;
+        const int64_t kblocks = (K / vw + kThreads - 1) / kThreads;
+        TPB_CHECK(O < 65536, "reduce_noalloc: %lld outer rows exceed the column kernel's grid",
+                  (long long)O);
+        int splits = 1;
+        const int64_t base_blocks = kblocks * O;
+        const int64_t want = int64_t(sms) * 4;
+        if (base_blocks < want) {
+            splits = static_cast<int>(std::min<int64_t>((want + base_blocks - 1) / base_blocks,
+                                                        std::max<int64_t>(R / 16, 1)));
+            splits = std::min(splits, 1024);
+        }
+        const int64_t rchunk = (R + splits - 1) / splits;
+        splits = static_cast<int>((R + rchunk - 1) / rchunk);
+        if (splits < 1) splits = 1;
+        if (splits > 1) check_noalloc_fit(sizeof(A) * splits * O * K);
+        dim3 grid(static_cast<unsigned>(kblocks), static_cast<unsigned>(O), static_cast<unsigned>(splits));
+        if (vec) {
+            reduce_cols<T, To, OP, V><<<grid, kThreads, 0, stream>>>(x, o, partial, O, R, K, os, rs,
+                                                                      rchunk, count);
+        } else {
+            reduce_cols<T, To, OP, 1><<<grid, kThreads, 0, stream>>>(x, o, partial, O, R, K, os, rs,
+                                                                      rchunk, count);
+        }
+        check_launch("reduce_cols");
+        if (splits > 1) {
+            const int64_t n = O * K;
+            const unsigned g2 = static_cast<unsigned>(std::min<int64_t>(blocks_for(n, kThreads), sms * 8));
+            reduce_col_partials<A, To, OP><<<g2, kThreads, 0, stream>>>(partial, o, n, splits, count);
+            check_launch("reduce_col_partials");
+        }
+        return;
+    }
+    const bool rows_ok = red.n == 0 || (red.n == 1 && red.strides[0] == 1);
+    TPB_CHECK(rows_ok,
+              "reduce_noalloc: the reduced dimensions are not laid out contiguously; this layout "
+              "needs a gathered copy of the input (%lld bytes), which the allocation-free entry "
+              "point does not make -- pass a contiguous input or use tp_b200_reduce",
+              (long long)(numel_of(xin) * (int64_t)sizeof(T)));
+    TPB_CHECK(rows < (int64_t(1) << 31), "reduce_noalloc: too many output elements");
+    const int which[1] = {0};
+    const auto calc = OffsetCalc<1>::make(group_layout(kept), which);
+    int splits = 1;
+    const int64_t want = int64_t(sms) * 4;
+    if (rows < want) {
+        splits = static_cast<int>(std::min<int64_t>((want + rows - 1) / rows,
+                                                    std::max<int64_t>(R / (kThreads * V * 4), 1)));
+    }
+    int64_t chunk = (R + splits - 1) / splits;
+    chunk = (chunk + V - 1) / V * V;
+    if (chunk < 1) chunk = 1;
+    splits = static_cast<int>(std::max<int64_t>((R + chunk - 1) / chunk, 1));
+    if (splits > 1) check_noalloc_fit(sizeof(A) * rows * splits);
+    reduce_rows<T, To, OP><<<static_cast<unsigned>(rows * splits), kThreads, 0, stream>>>(
+        x, o, partial, calc, R, splits, chunk, count);
+    check_launch("reduce_rows");
+    if (splits > 1) {
+        reduce_row_partials<A, To, OP><<<static_cast<unsigned>(rows), kThreads, 0, stream>>>(
+            partial, o, splits, count);
+        check_launch("reduce_row_partials");
+    }
+}
+
+template <typename T, int OP>
+void reduce_noalloc_out(const tpb_tensor& out, const tpb_tensor& x, uint32_t mask, int dev,
+                        cudaStream_t stream, void* scratch) {
+    using A = typename Acc<T>::type;
+    if (out.dtype == x.dtype) {
+        reduce_launch_noalloc<T, T, OP>(out, x, mask, dev, stream, scratch);
+    } else if (out.dtype == AccCode<A>::value) {
+        reduce_launch_noalloc<T, A, OP>(out, x, mask, dev, stream, scratch);
+    } else {
+        TPB_CHECK(false, "reduce_noalloc: a %s result of a %s input needs a conversion buffer; use "
+                  "tp_b200_reduce", dtype_name(out.dtype), dtype_name(x.dtype));
+    }
+}
+
+template <typename T>
+void reduce_noalloc_op(int op, const tpb_tensor& out, const tpb_tensor& x, uint32_t mask, int dev,
+                       cudaStream_t stream, void* scratch) {
+    switch (op) {
+        case TPB_SUM: reduce_noalloc_out<T, TPB_SUM>(out, x, mask, dev, stream, scratch); break;
+        case TPB_MEAN: reduce_noalloc_out<T, TPB_MEAN>(out, x, mask, dev, stream, scratch); break;
+        case TPB_AMAX: reduce_launch_noalloc<T, T, TPB_AMAX>(out, x, mask, dev, stream, scratch); break;
+        case TPB_AMIN: reduce_launch_noalloc<T, T, TPB_AMIN>(out, x, mask, dev, stream, scratch); break;
+        default: TPB_CHECK(false, "reduce_noalloc: unknown op %d", op);
+    }
+}
+
+}  // namespace
+}  // namespace tpb
+
 using namespace tpb;
+
+extern "C" {
+
+int tp_b200_reduce_noalloc(int op, const tpb_tensor* out, const tpb_tensor* x, uint32_t dim_mask,
+                           void* stream) {
+    return guarded([&] {
+        check_tensor(out, "reduce_noalloc out");
+        check_tensor(x, "reduce_noalloc input");
+        TPB_CHECK(out->ndim == x->ndim, "reduce_noalloc: the output keeps every dimension (keepdim layout)");
+        TPB_CHECK(x->ndim == 0 || (dim_mask >> x->ndim) == 0, "reduce_noalloc: dimension mask out of range");
+        for (int i = 0; i < x->ndim; ++i) {
+            const int64_t want = (dim_mask >> i) & 1 ? 1 : x->sizes[i];
+            TPB_CHECK(out->sizes[i] == want, "reduce_noalloc: output size %lld at dimension %d, expected %lld",
+                      (long long)out->sizes[i], i, (long long)want);
+        }
+        TPB_CHECK(is_contiguous(*out), "reduce_noalloc: the output must be contiguous");
+        if (op == TPB_AMAX || op == TPB_AMIN) {
+            TPB_CHECK(out->dtype == x->dtype, "amax/amin: output dtype must match the input");
+        }
+        if (numel_of(*out) == 0) return;
+        TPB_CHECK(numel_of(*x) > 0, "reduce_noalloc: empty reductions are not supported here; use tp_b200_reduce");
+        const int dev = device_of(out->data);
+        DeviceGuard guard(dev);
+        cudaStream_t s = resolve_stream(stream, dev);
+        void* scratch = noalloc_scratch(dev);
+        TPB_DISPATCH_ALL(x->dtype, "reduce_noalloc",
+                         { reduce_noalloc_op<scalar_t>(op, *out, *x, dim_mask, dev, s, scratch); });
+    });
+}
+
+}  // extern "C"
 
 extern "C" {
 
