@@ -80,7 +80,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -453,6 +453,52 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     host.close()
 
 
+def run_only(args) -> None:
+    """One kernel's workload, `--steps` launches (for ncu captures of a single kernel)."""
+    torch.cuda.set_device(0)
+    import tensorplay_mlu_b200 as tpb
+
+    tpb.load()
+    ops = tpb.ops
+    g = torch.Generator(device="cuda").manual_seed(0)
+
+    def rnd(*shape, dt=torch.bfloat16, scale=1.0):
+        return (torch.randn(*shape, generator=g, device="cuda") * scale).to(dt)
+
+    name = args.only
+    if name == "gemm_mlp":        # the MLP's forward GEMM: [8192,4096] @ W1[16384,4096]^T
+        a, w = rnd(8192, 4096), rnd(16384, 4096, scale=4096 ** -0.5)
+        fn = lambda: ops.linear(a, w)
+    elif name == "gemm_mlp_dw":   # weight-gradient GEMM: d_out^T [4096,8192] @ a [8192,16384]
+        a, b = rnd(8192, 4096), rnd(8192, 16384)
+        fn = lambda: ops.mm(a.t(), b)
+    elif name == "gemm_mm8192":
+        a, b = rnd(8192, 8192, scale=8192 ** -0.5), rnd(8192, 8192)
+        fn = lambda: ops.mm(a, b)
+    elif name == "bmm":
+        a, b = rnd(64, 2048, 128, scale=128 ** -0.5), rnd(64, 128, 2048)
+        fn = lambda: ops.bmm(a, b)
+    elif name == "gelu_bf16":
+        a = rnd(8192, 8192)
+        fn = lambda: ops.gelu(a)
+    elif name == "sum_bf16":
+        a = rnd(8192, 8192)
+        fn = lambda: ops.sum(a)
+    elif name == "softmax_bf16":
+        a = rnd(32768, 4096)
+        fn = lambda: ops.softmax(a, -1)
+    elif name == "add_row_f32":
+        a, b = rnd(8192, 8192, dt=torch.float32), rnd(8192, dt=torch.float32)
+        fn = lambda: ops.add_Tensor(a, b)
+    else:
+        raise SystemExit(f"unknown --only workload {name}")
+    for _ in range(args.steps):
+        fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"only": name, "launches": args.steps,
+                      "device_error": tpb._native.lib().tp_b200_take_device_error(0)}))
+
+
 class _PrefixStore:
     """Keys of the NCCL rendezvous under their own prefix in the job store."""
 
@@ -472,11 +518,16 @@ class _PrefixStore:
 def main() -> None:
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
-    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-extras", action="store_true", help="skip the op sweep, GEMM set and CPU baseline")
+    p.add_argument("--only", default=None,
+                   help="run one kernel workload --steps times and exit (for ncu captures)")
     args = p.parse_args()
+    if args.only:
+        run_only(args)
+        return
     if args.warmup < 3:
         args.warmup = 3
     rank, world, local = dist_env()
