@@ -34,6 +34,8 @@
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -491,6 +493,361 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ------------------------------------------------- 2-SM (CTA pair) kernel --
+//
+// A cluster of two CTAs on two SMs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M = 256): each CTA stages its own 128 rows of A
+// and its own 128 columns of B (32 KiB per 64-deep K step instead of 48 KiB
+// for a 128 x 256 tile on one SM, so 6 stages fit and L2 traffic per flop
+// drops by a third), the leader CTA's single MMA thread drives both SMs'
+// tensor cores, and each CTA's TMEM holds its 128 output rows.
+//   * Both CTAs' TMA loads (.cta_group::2, no multicast) complete on the
+//     leader's "full" barrier, which only the leader arms, with the pair's
+//     total bytes.
+//   * The leader's commits are multicast to the same barrier in both CTAs:
+//     "empty" (the stage may be refilled in both) and "acc_full".
+//   * Both CTAs' epilogue warps arrive on the leader's "acc_empty" (count 8).
+// Waits are bounded as in the 1-SM kernel; teardown is a cluster barrier
+// followed by the paired TMEM release.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Shared::cluster address of the variable at `local_addr` in CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_cta(uint32_t local_addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                                 int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                                 int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+
+template <bool TF32>
+__device__ __forceinline__ void umma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+    if constexpr (TF32) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+            : "memory");
+    }
+}
+
+// Arrive on the barrier at `bar`'s offset in both CTAs of the pair once the
+// MMAs issued so far are done.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+    const uint16_t mask = 0x3;
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+        "h"(mask)
+        : "memory");
+}
+
+constexpr int kPairStages = 6;
+constexpr int kPairBM = 256;  // rows per CTA pair (128 per CTA)
+constexpr int kPairBN = 256;  // columns per CTA pair (each CTA stages 128 of B)
+
+template <typename T>
+constexpr size_t tc2_smem_bytes() {
+    return size_t(kPairStages) * (128 * 128 + 128 * 128) + 1024 + 256;
+}
+
+__device__ __forceinline__ void tile_coords_pair(const TcParams& p, int tile, int& b, int& mt, int& nt,
+                                                 int group_m) {
+    const int per_batch = p.m_tiles * p.n_tiles;
+    b = tile / per_batch;
+    const int r = tile - b * per_batch;
+    const int group = group_m * p.n_tiles;
+    const int g = r / group;
+    const int first_m = g * group_m;
+    const int gsize = min(p.m_tiles - first_m, group_m);
+    const int q = r - g * group;
+    mt = first_m + q % gsize;
+    nt = q / gsize;
+}
+
+template <typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const TcParams p, const int group_m) {
+    using E = TcElem<T>;
+    constexpr int kStages = kPairStages;
+    constexpr int kTmemCols = 2 * kPairBN;
+    constexpr int kEPR = 128 / E::kES;
+    constexpr int kUmmaK = 32 / E::kES;
+    constexpr int kKSteps = kEPR / kUmmaK;
+    constexpr uint32_t kABytes = 128 * 128;   // this CTA's 128 rows of A
+    constexpr uint32_t kBBytes = 128 * 128;   // this CTA's 128 columns of B
+    constexpr uint32_t kChunk = kEPR * 128;
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* smem_a = smem;
+    uint8_t* smem_b = smem + kStages * kABytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_b + kStages * kBBytes);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + kStages;
+    uint64_t* acc_full = bars + 2 * kStages;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* drain = acc_empty + 2;
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int cluster_id = blockIdx.x >> 1;
+    const int num_clusters = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(smem_addr(&full[s]), 1);
+            mbar_init(smem_addr(&empty[s]), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(smem_addr(&acc_full[a]), 1);
+            mbar_init(smem_addr(&acc_empty[a]), 8);
+        }
+        mbar_init(smem_addr(drain), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_addr(const_cast<uint32_t*>(tmem_slot)), kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------------------------------------------- producer --
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int tile = cluster_id; tile < p.num_tiles && ok; tile += num_clusters) {
+                int b, mt, nt;
+                tile_coords_pair(p, tile, b, mt, nt, group_m);
+                const int m0 = mt * kPairBM + int(rank) * 128;
+                const int n0 = nt * kPairBN + int(rank) * 128;
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait(smem_addr(&empty[stage]), phase ^ 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t own_full = smem_addr(&full[stage]);
+                    if (leader) mbar_expect_tx(own_full, 2 * (kABytes + kBBytes));
+                    const uint32_t fb = map_to_cta(own_full, 0);  // the leader's barrier
+                    const uint32_t da = smem_addr(smem_a + stage * kABytes);
+                    const uint32_t db = smem_addr(smem_b + stage * kBBytes);
+                    const int k0 = kb * kEPR;
+                    if (p.a_mn) {
+                        for (int j = 0; j < 128 / kEPR; ++j) {
+                            if (p.batched) tma_load_3d_pair(da + j * kChunk, &tmA, fb, m0 + j * kEPR, k0, b);
+                            else tma_load_2d_pair(da + j * kChunk, &tmA, fb, m0 + j * kEPR, k0);
+                        }
+                    } else {
+                        if (p.batched) tma_load_3d_pair(da, &tmA, fb, k0, m0, b);
+                        else tma_load_2d_pair(da, &tmA, fb, k0, m0);
+                    }
+                    if (p.b_mn) {
+                        for (int j = 0; j < 128 / kEPR; ++j) {
+                            if (p.batched) tma_load_3d_pair(db + j * kChunk, &tmB, fb, n0 + j * kEPR, k0, b);
+                            else tma_load_2d_pair(db + j * kChunk, &tmB, fb, n0 + j * kEPR, k0);
+                        }
+                    } else {
+                        if (p.batched) tma_load_3d_pair(db, &tmB, fb, k0, n0, b);
+                        else tma_load_2d_pair(db, &tmB, fb, k0, n0);
+                    }
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            if (!ok) atomicExch(p.err, kErrProducer);
+        }
+    } else if (warp == 1) {
+        // ----------------------------------- MMA issuer (leader CTA only) --
+        if (leader && lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            bool ok = true;
+            const uint32_t a_lbo = p.a_mn ? kChunk : 16;
+            const uint32_t b_lbo = p.b_mn ? kChunk : 16;
+            const uint32_t a_kstep = p.a_mn ? kUmmaK * 128 : 32;
+            const uint32_t b_kstep = p.b_mn ? kUmmaK * 128 : 32;
+            for (int tile = cluster_id; tile < p.num_tiles && ok; tile += num_clusters, ++local) {
+                const int acc = local & 1;
+                const uint32_t acc_phase = (local >> 1) & 1;
+                if (!mbar_wait(smem_addr(&acc_empty[acc]), acc_phase ^ 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * kPairBN;
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait(smem_addr(&full[stage]), phase, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_addr(smem_a + stage * kABytes);
+                    const uint32_t sb = smem_addr(smem_b + stage * kBBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kKSteps; ++kk) {
+                        const uint64_t ad = sw128_desc(sa + kk * a_kstep, a_lbo, 1024);
+                        const uint64_t bd = sw128_desc(sb + kk * b_kstep, b_lbo, 1024);
+                        umma_pair<E::kTF32>(d_tmem, ad, bd, p.idesc, (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    umma_commit_pair(smem_addr(&empty[stage]));
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                umma_commit_pair(smem_addr(&acc_full[acc]));
+            }
+            if (!ok) atomicExch(p.err, kErrMma);
+            // Drain with a commit of the same CTA-group as the MMAs (it also
+            // arrives, unobserved, on the peer's drain barrier).
+            umma_commit_pair(smem_addr(drain));
+            const uint64_t start = global_ns();
+            while (!mbar_try_wait(smem_addr(drain), 0)) {
+                if (global_ns() - start > kWaitNs) break;
+            }
+        }
+    } else {
+        // ------------------------------------------ epilogue (both CTAs) --
+        const int quad = warp & 3;
+        const int row_in_tile = int(rank) * 128 + quad * 32 + lane;
+        int local = 0;
+        T* c = static_cast<T*>(p.c);
+        const T* cin = static_cast<const T*>(p.cin);
+        const uint32_t leader_empty0 = map_to_cta(smem_addr(&acc_empty[0]), 0);
+        const uint32_t leader_empty1 = map_to_cta(smem_addr(&acc_empty[1]), 0);
+        for (int tile = cluster_id; tile < p.num_tiles; tile += num_clusters, ++local) {
+            const int acc = local & 1;
+            const uint32_t acc_phase = (local >> 1) & 1;
+            if (!mbar_wait(smem_addr(&acc_full[acc]), acc_phase, abort_flag)) {
+                if (lane == 0) atomicExch(p.err, kErrEpilogue);
+                break;
+            }
+            tc_fence_after();
+            int b, mt, nt;
+            tile_coords_pair(p, tile, b, mt, nt, group_m);
+            const int64_t gm = int64_t(mt) * kPairBM + row_in_tile;
+            const bool row_ok = gm < p.M;
+            T* crow = c + b * p.sc_b + gm * p.sc_m;
+            const uint32_t t_base = tmem_base + (uint32_t(quad * 32) << 16) + acc * kPairBN;
+#pragma unroll 1
+            for (int chunk = 0; chunk < kPairBN / 32; ++chunk) {
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld32(t_base + chunk * 32, r);
+                tmem_wait_ld();
+                const int64_t n_base = int64_t(nt) * kPairBN + chunk * 32;
+                if (row_ok && n_base < p.N) {
+                    float v[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
+                    if (cin != nullptr) {
+                        const T* crow_in = cin + b * p.sci_b + gm * p.sci_m;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (n_base + j < p.N) v[j] += p.beta * load_as<float>(crow_in[(n_base + j) * p.sci_n]);
+                        }
+                    }
+                    if (p.vec_store && n_base + 32 <= p.N) {
+                        constexpr int V = 16 / sizeof(T);
+#pragma unroll
+                        for (int j = 0; j < 32; j += V) {
+                            Vec<T, V> o;
+#pragma unroll
+                            for (int q = 0; q < V; ++q) o.v[q] = store_as<T>(v[j + q]);
+                            *reinterpret_cast<Vec<T, V>*>(crow + n_base + j) = o;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (n_base + j < p.N) crow[n_base + j] = store_as<T>(v[j]);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc == 0 ? leader_empty0 : leader_empty1);
+        }
+    }
+
+    // Teardown: every thread of both CTAs reaches this point (no early
+    // returns), so the cluster barrier completes; TMEM is then released
+    // pairwise.
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, kTmemCols);
+    }
+}
+
 // ------------------------------------------------------------ host side --
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -582,6 +939,41 @@ void launch_tc(const GemmProblem& p, const CUtensorMap& ma, const CUtensorMap& m
 }
 
 template <typename T>
+void launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, TcParams& tp, int dev, cudaStream_t stream) {
+    constexpr size_t smem = tc2_smem_bytes<T>();
+    static bool configured[64] = {};
+    if (!configured[dev]) {
+        TPB_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(smem)));
+        configured[dev] = true;
+    }
+    tp.m_tiles = (tp.M + kPairBM - 1) / kPairBM;
+    tp.n_tiles = (tp.N + kPairBN - 1) / kPairBN;
+    tp.num_tiles = tp.batch * tp.m_tiles * tp.n_tiles;
+    const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : std::is_same<T, float>::value ? 2u : 0u;
+    tp.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (uint32_t(tp.a_mn) << 15) |
+               (uint32_t(tp.b_mn) << 16) | (uint32_t(kPairBN >> 3) << 17) | (uint32_t(kPairBM >> 4) << 24);
+    // Row-tile groups sized so the group's A panels (~64 MiB) stay in L2
+    // while B streams past them once.
+    const int64_t panel = int64_t(kPairBM) * tp.K * int64_t(sizeof(T));
+    int group_m = static_cast<int>(std::max<int64_t>(1, (int64_t(64) << 20) / std::max<int64_t>(panel, 1)));
+    group_m = std::min(group_m, tp.m_tiles);
+    const int clusters = std::min(tp.num_tiles, num_sms(dev) / 2);
+    gemm_tc2_kernel<T><<<2 * clusters, kThreads, smem, stream>>>(ma, mb, tp, group_m);
+    check_launch("gemm_tc2");
+}
+
+// Which kernel: the CTA-pair kernel for problems with at least one full
+// 256 x 256 tile, the single-SM kernel otherwise; TPB200_GEMM_KERNEL=1sm|2sm
+// overrides the choice (for A/B measurements).
+bool use_pair_kernel(const GemmProblem& p) {
+    static const char* force = std::getenv("TPB200_GEMM_KERNEL");
+    if (force != nullptr && std::strcmp(force, "1sm") == 0) return false;
+    if (force != nullptr && std::strcmp(force, "2sm") == 0) return true;
+    return p.M >= kPairBM && p.N >= kPairBN;
+}
+
+template <typename T>
 bool gemm_tc_typed(const GemmProblem& p_in, int dev, cudaStream_t stream, CUtensorMapDataType type) {
     constexpr int es = sizeof(T);
     GemmProblem p = p_in;
@@ -646,9 +1038,11 @@ bool gemm_tc_typed(const GemmProblem& p_in, int dev, cudaStream_t stream, CUtens
     if (!tma_ok(p.b, es, b_k ? p.sb_n : p.sb_k, p.batch, p.sb_b)) return false;
     if (p.M >= (int64_t(1) << 31) || p.N >= (int64_t(1) << 31) || p.K >= (int64_t(1) << 31)) return false;
     const int sms = num_sms(dev);
-    const int bn = choose_bn(p.M, p.N, p.batch, sms);
+    const bool pair = use_pair_kernel(p);
+    const int bn = pair ? 128 : choose_bn(p.M, p.N, p.batch, sms);  // B rows staged per CTA
     constexpr int kEPR = 128 / es;
-    // A box: K-major 64 x 128 rows; M-major 64 (M) x 64 (K) chunks.
+    // A box: K-major 64 x 128 rows; M-major 64 (M) x 64 (K) chunks.  B box:
+    // K-major 64 x bn rows; N-major 64 x 64 chunks.
     const CUtensorMap ma = a_k ? make_map(p.a, type, es, p.K, p.M, p.sa_m, p.batch, p.sa_b, kBM)
                                : make_map(p.a, type, es, p.M, p.K, p.sa_k, p.batch, p.sa_b, kEPR);
     const CUtensorMap mb = b_k ? make_map(p.b, type, es, p.K, p.N, p.sb_n, p.batch, p.sb_b, bn)
@@ -673,7 +1067,8 @@ bool gemm_tc_typed(const GemmProblem& p_in, int dev, cudaStream_t stream, CUtens
     tp.beta = static_cast<float>(p.beta);
     tp.vec_store = aligned16(p.c) && (p.sc_m * es) % 16 == 0 && (p.batch == 1 || (p.sc_b * es) % 16 == 0);
     tp.err = device_error_word(dev);
-    if (bn == 256) launch_tc<T, 256>(p, ma, mb, tp, dev, stream);
+    if (pair) launch_tc2<T>(ma, mb, tp, dev, stream);
+    else if (bn == 256) launch_tc<T, 256>(p, ma, mb, tp, dev, stream);
     else launch_tc<T, 128>(p, ma, mb, tp, dev, stream);
     return true;
 }

@@ -72,6 +72,25 @@ def test_tensor_core_transposes(ops, dtype, ta, tb):
     assert_close(ops.mm(da, db), O.gemm(a, b), dtype, scale=K ** 0.5)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True), (True, True)])
+def test_cta_pair_kernel_transposes_and_tails(ops, dtype, ta, tb):
+    # M, N >= 256 take the 2-SM (cta_group::2) kernel: 256 x 256 tiles with
+    # tails in M, N and K, every operand major, and a batched case.
+    M, N, K = 520, 776, 200
+    a, b = rand(M, K, dtype=dtype, seed=1), rand(K, N, dtype=dtype, seed=2)
+    da = dev(ops, a.t().contiguous()).t() if ta else dev(ops, a)
+    db = dev(ops, b.t().contiguous()).t() if tb else dev(ops, b)
+    assert_close(ops.mm(da, db), O.gemm(a, b), dtype, scale=K ** 0.5)
+    x, y = rand(3, 300, 136, dtype=dtype, seed=3), rand(3, 136, 264, dtype=dtype, seed=4)
+    dx_ = dev(ops, x.transpose(1, 2).contiguous()).transpose(1, 2) if ta else dev(ops, x)
+    dy_ = dev(ops, y.transpose(1, 2).contiguous()).transpose(1, 2) if tb else dev(ops, y)
+    assert_close(ops.bmm(dx_, dy_), O.gemm(x, y), dtype, scale=136 ** 0.5)
+    bias = rand(N, dtype=dtype, seed=5)
+    assert_close(ops.addmm(dev(ops, bias), da, db, beta=1.0, alpha=0.5),
+                 O.gemm(a, b, bias, 0.5, 1.0), dtype, scale=K ** 0.5)
+
+
 @pytest.mark.parametrize("dtype", [torch.int32, torch.int64, torch.int8])
 def test_integer_mm_is_exact(ops, dtype):
     g = torch.Generator().manual_seed(0)
