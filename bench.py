@@ -313,14 +313,59 @@ def gemm_set(ops, bf16_peak: float):
     return res
 
 
+def collective_sweep(pg, host, ops, world: int, max_bytes: int = 1 << 30):
+    """BASELINE config 5b: NCCL collectives through the nccl_b200 process group,
+    bus bandwidth by the nccl-tests convention (all_reduce 2(n-1)/n, others
+    (n-1)/n), time = max over ranks of CUDA-event time."""
+    res = {}
+    sizes = []
+    s = 4096
+    while s <= max_bytes:
+        sizes.append(s)
+        s *= 4
+    for dt, tag in ((torch.float32, "f32"), (torch.bfloat16, "bf16")):
+        es = torch.finfo(dt).bits // 8
+        for nbytes in sizes:
+            n = (nbytes // es) // world * world
+            buf = torch.ones(n, dtype=dt, device="cuda")
+            out = torch.empty(n, dtype=dt, device="cuda")
+            part = torch.empty(n // world, dtype=dt, device="cuda")
+            cases = {
+                "all_reduce": (lambda: pg.allreduce([buf], 0), 2.0 * (world - 1) / world),
+                "all_gather": (lambda: pg.all_gather_single(out, buf[: n // world]), (world - 1) / world),
+                "reduce_scatter": (lambda: pg.reduce_scatter_single(part, buf, 0), (world - 1) / world),
+                "all_to_all": (lambda: pg.all_to_all_single(out, buf), (world - 1) / world),
+            }
+            for name, (fn, factor) in cases.items():
+                iters = 5 if nbytes >= (64 << 20) else 20
+                for _ in range(2):
+                    fn()
+                torch.cuda.synchronize()
+                host.barrier()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(iters):
+                    fn()
+                e1.record()
+                e1.synchronize()
+                ms = host.max(e0.elapsed_time(e1) / iters)
+                algbw = n * es / (ms * 1e-3) / 1e9
+                res.setdefault(f"{name}_{tag}", []).append(
+                    {"bytes": n * es, "ms": round(ms, 4), "algbw_gb_s": round(algbw, 1),
+                     "busbw_gb_s": round(algbw * factor, 1)})
+            del buf, out, part
+    return res
+
+
 def run_ours(args, rank: int, world: int, local: int) -> None:
-    torch.cuda.set_device(local)
     import tensorplay_mlu_b200 as tpb
     from tensorplay_mlu_b200 import _native as N
     from tensorplay_mlu_b200 import distributed as D
     from tensorplay_mlu_b200.train import DataParallelMLP, MLPConfig, init_params_host, make_batch_host
 
-    tpb.load()
+    tpb.load()  # before any CUDA call, so the caching allocator backs every tensor
+    assert tpb.allocator_installed(), "the B200 caching allocator must back the benchmark's tensors"
+    torch.cuda.set_device(local)
     ops = tpb.ops
     host = HostGroup(rank, world)
     hbm_peak, bf16_peak, bf16_sustained, peak_kind = peaks()
@@ -435,6 +480,12 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     del x, t, bufs
     if pg is not None:
         torch.cuda.synchronize()
+        if not args.no_extras:
+            sweep = collective_sweep(pg, host, ops, world)
+            if rank == 0:
+                line["collectives"] = sweep
+        torch.cuda.synchronize()
+        host.barrier()
         pg.destroy()
     if rank == 0 and world == 1 and not args.no_extras:
         del model
@@ -455,10 +506,10 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
 
 def run_only(args) -> None:
     """One kernel's workload, `--steps` launches (for ncu captures of a single kernel)."""
-    torch.cuda.set_device(0)
     import tensorplay_mlu_b200 as tpb
 
     tpb.load()
+    torch.cuda.set_device(0)
     ops = tpb.ops
     g = torch.Generator(device="cuda").manual_seed(0)
 

@@ -9,10 +9,12 @@
  * tp_b200_last_error() (thread-local).
  *
  * Device pointers belong to the caller.  Every operator entry point is
- * asynchronous: it enqueues work on `stream` (a cudaStream_t; NULL selects the
- * library's current stream for the tensor's device, see tp_b200_set_stream)
- * and returns.  Each operator declaration names the tensorplay-mlu kernel it
- * replaces (path within the reference project, file:line).
+ * asynchronous: it enqueues work on `stream` (a cudaStream_t; NULL is the CUDA
+ * default stream) and returns.  Entry points whose reference signature has
+ * no stream argument (the collectives) use the calling thread's current
+ * stream of the device, set with tp_b200_set_stream.  Each operator
+ * declaration names the tensorplay-mlu kernel it replaces (path within the
+ * reference project, file:line).
  */
 #ifndef TPB200_H
 #define TPB200_H
@@ -71,9 +73,9 @@ int tp_b200_set_device(int dev);
 int tp_b200_capability(int dev);
 /* MLURuntime.cpp:107-110 synchronize: blocks until the device is idle. */
 int tp_b200_synchronize(int dev);
-/* MLURuntime.cpp:81-93 queue(index).  The stream that entry points given a
- * NULL stream use on `dev`, per calling thread.  Defaults to the legacy
- * default stream (0), the stream PyTorch also starts on. */
+/* MLURuntime.cpp:81-93 queue(index).  The stream the collectives of this
+ * thread are ordered on for `dev`.  Defaults to the CUDA default stream (0),
+ * the stream PyTorch also starts on. */
 int tp_b200_set_stream(int dev, void* stream);
 void* tp_b200_get_stream(int dev);
 /* MLURuntime.cpp:112-136 copy_to_device / copy_to_host / copy_on_device and

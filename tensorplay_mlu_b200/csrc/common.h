@@ -73,8 +73,12 @@ const char* dtype_name(int dtype);
 
 // The device a pointer lives on (the current device for host pointers).
 int device_of(const void* ptr);
-// Resolve NULL to the thread's current stream of `dev`.
+// The stream an operator runs on: its argument as given (NULL = the CUDA
+// default stream).
 cudaStream_t resolve_stream(void* stream, int dev);
+// The calling thread's current stream of `dev` (tp_b200_set_stream), used by
+// the entry points whose reference signature carries no stream (collectives).
+cudaStream_t thread_current_stream(int dev);
 int num_sms(int dev);
 // Per-device word that kernels with bounded waits write a failure code into.
 int* device_error_word(int dev);

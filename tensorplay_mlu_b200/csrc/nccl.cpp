@@ -11,6 +11,7 @@
 #include <cstring>
 #include <string>
 #include <thread>
+#include <vector>
 
 #include "common.h"
 
@@ -82,7 +83,41 @@ int nccl_guarded(F&& body) {
     }
 }
 
-cudaStream_t comm_stream(int dev) { return resolve_stream(nullptr, dev); }
+cudaStream_t comm_stream(int dev) { return thread_current_stream(dev); }
+
+// Communicators are created non-blocking (so creation can be bounded by a
+// timeout), and a non-blocking communicator may answer a call with
+// ncclInProgress; NCCL then requires polling its asynchronous state until it
+// settles before the next call on it.  Inside a group the settling happens
+// once, for every communicator the group touched, at group end.
+thread_local int g_group_depth = 0;
+thread_local std::vector<ncclComm_t> g_group_comms;
+constexpr int kSettleMs = 120000;
+
+void settle(ncclComm_t comm, const char* what) {
+    ncclResult_t state = ncclInProgress;
+    const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(kSettleMs);
+    while (true) {
+        check(ncclCommGetAsyncError(comm, &state), "commGetAsyncError");
+        if (state != ncclInProgress) break;
+        if (std::chrono::steady_clock::now() > deadline) {
+            throw Error(format("NCCL: %s did not settle within %d ms", what, kSettleMs));
+        }
+        std::this_thread::yield();
+    }
+    if (state != ncclSuccess) throw Error(format("NCCL error: %s (%s)", ncclGetErrorString(state), what));
+}
+
+// Issue one NCCL call on `comm`: check its status and settle it (or record
+// the communicator for the enclosing group).
+void run(ncclComm_t comm, ncclResult_t status, const char* what) {
+    check(status, what);
+    if (g_group_depth > 0) {
+        g_group_comms.push_back(comm);
+        return;
+    }
+    if (status == ncclInProgress) settle(comm, what);
+}
 
 }  // namespace
 }  // namespace tpb
@@ -187,7 +222,7 @@ int tp_b200_nccl_all_reduce(const void* send, void* recv, size_t count, int dtyp
         const ncclDataType_t t = type_of(dtype);
         const ncclRedOp_t o = op_of(op);
         DeviceGuard guard(dev);
-        check(ncclAllReduce(send, recv, count, t, o, c, comm_stream(dev)), "allReduce");
+        run(c, ncclAllReduce(send, recv, count, t, o, c, comm_stream(dev)), "allReduce");
     });
 }
 
@@ -197,7 +232,7 @@ int tp_b200_nccl_broadcast(const void* send, void* recv, size_t count, int dtype
         ncclComm_t c = as_comm(comm);
         const ncclDataType_t t = type_of(dtype);
         DeviceGuard guard(dev);
-        check(ncclBroadcast(send, recv, count, t, root, c, comm_stream(dev)), "broadcast");
+        run(c, ncclBroadcast(send, recv, count, t, root, c, comm_stream(dev)), "broadcast");
     });
 }
 
@@ -208,7 +243,7 @@ int tp_b200_nccl_reduce(const void* send, void* recv, size_t count, int dtype, i
         const ncclDataType_t t = type_of(dtype);
         const ncclRedOp_t o = op_of(op);
         DeviceGuard guard(dev);
-        check(ncclReduce(send, recv, count, t, o, root, c, comm_stream(dev)), "reduce");
+        run(c, ncclReduce(send, recv, count, t, o, root, c, comm_stream(dev)), "reduce");
     });
 }
 
@@ -217,7 +252,7 @@ int tp_b200_nccl_all_gather(const void* send, void* recv, size_t count, int dtyp
         ncclComm_t c = as_comm(comm);
         const ncclDataType_t t = type_of(dtype);
         DeviceGuard guard(dev);
-        check(ncclAllGather(send, recv, count, t, c, comm_stream(dev)), "allGather");
+        run(c, ncclAllGather(send, recv, count, t, c, comm_stream(dev)), "allGather");
     });
 }
 
@@ -228,7 +263,7 @@ int tp_b200_nccl_reduce_scatter(const void* send, void* recv, size_t count, int 
         const ncclDataType_t t = type_of(dtype);
         const ncclRedOp_t o = op_of(op);
         DeviceGuard guard(dev);
-        check(ncclReduceScatter(send, recv, count, t, o, c, comm_stream(dev)), "reduceScatter");
+        run(c, ncclReduceScatter(send, recv, count, t, o, c, comm_stream(dev)), "reduceScatter");
     });
 }
 
@@ -247,7 +282,7 @@ int tp_b200_nccl_all_to_all(const void* send, void* recv, size_t count, int dtyp
             check(ncclSend(static_cast<const char*>(send) + peer * count * es, count, t, peer, c, s), "send");
             check(ncclRecv(static_cast<char*>(recv) + peer * count * es, count, t, peer, c, s), "recv");
         }
-        check(ncclGroupEnd(), "groupEnd");
+        run(c, ncclGroupEnd(), "allToAll");
     });
 }
 
@@ -256,7 +291,7 @@ int tp_b200_nccl_send(const void* buf, size_t count, int dtype, int peer, int de
         ncclComm_t c = as_comm(comm);
         const ncclDataType_t t = type_of(dtype);
         DeviceGuard guard(dev);
-        check(ncclSend(buf, count, t, peer, c, comm_stream(dev)), "send");
+        run(c, ncclSend(buf, count, t, peer, c, comm_stream(dev)), "send");
     });
 }
 
@@ -265,16 +300,28 @@ int tp_b200_nccl_recv(void* buf, size_t count, int dtype, int peer, int dev, voi
         ncclComm_t c = as_comm(comm);
         const ncclDataType_t t = type_of(dtype);
         DeviceGuard guard(dev);
-        check(ncclRecv(buf, count, t, peer, c, comm_stream(dev)), "recv");
+        run(c, ncclRecv(buf, count, t, peer, c, comm_stream(dev)), "recv");
     });
 }
 
 int tp_b200_nccl_group_start(void) {
-    return nccl_guarded([&] { check(ncclGroupStart(), "groupStart"); });
+    return nccl_guarded([&] {
+        check(ncclGroupStart(), "groupStart");
+        ++g_group_depth;
+    });
 }
 
 int tp_b200_nccl_group_end(void) {
-    return nccl_guarded([&] { check(ncclGroupEnd(), "groupEnd"); });
+    return nccl_guarded([&] {
+        if (g_group_depth > 0) --g_group_depth;
+        const ncclResult_t status = ncclGroupEnd();
+        check(status, "groupEnd");
+        if (g_group_depth == 0) {
+            std::vector<ncclComm_t> comms;
+            comms.swap(g_group_comms);
+            for (ncclComm_t c : comms) settle(c, "groupEnd");
+        }
+    });
 }
 
 int tp_b200_nccl_synchronize(int dev) {

@@ -77,7 +77,14 @@ int device_of(const void* ptr) {
 }
 
 cudaStream_t resolve_stream(void* stream, int dev) {
-    if (stream != nullptr) return static_cast<cudaStream_t>(stream);
+    (void)dev;
+    // An operator's stream argument is taken as given: NULL is the CUDA
+    // default stream, which is also the handle PyTorch reports for its
+    // default stream.
+    return static_cast<cudaStream_t>(stream);
+}
+
+cudaStream_t thread_current_stream(int dev) {
     TPB_CHECK(dev >= 0 && dev < kMaxDevices, "invalid device index %d", dev);
     return g_streams[dev];
 }
