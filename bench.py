@@ -212,10 +212,14 @@ def time_events(fn, iters: int, warmup: int = 3) -> float:
     return start.elapsed_time(end) / iters
 
 
-def op_sweep(ops, hbm_peak: float):
+def op_sweep(ops, hbm_peak: float, iters: int = 10):
     """memory-bound kernels, achieved GB/s and fraction of HBM."""
     g = torch.Generator(device="cuda").manual_seed(0)
     res = {}
+    _time_events = globals()["time_events"]
+
+    def time_events(fn, n):  # noqa: F811 -- the sweep's own iteration count
+        return _time_events(fn, iters)
 
     def record(name, ms, nbytes):
         gbs = nbytes / (ms * 1e-3) / 1e9
@@ -304,8 +308,9 @@ def gemm_set(ops, bf16_peak: float):
     prev = torch.get_float32_matmul_precision()
     torch.set_float32_matmul_precision("highest")
     try:
-        simt_peak = 148 * 128 * 2 * 1.965e9 / 1e12
-        record("mm_4096_fp32_highest", time_events(lambda: ops.mm(fa, fb), 5), 2 * n ** 3, simt_peak)
+        # Full fp32 precision runs as three TF32 tensor-core products (the
+        # split-precision method): its ceiling is a third of the TF32 peak.
+        record("mm_4096_fp32_highest", time_events(lambda: ops.mm(fa, fb), 5), 2 * n ** 3, bf16_peak / 2 / 3)
         torch.set_float32_matmul_precision("high")
         record("mm_4096_fp32_tf32", time_events(lambda: ops.mm(fa, fb), 10), 2 * n ** 3, bf16_peak / 2)
     finally:
@@ -532,9 +537,15 @@ def run_only(args) -> None:
     elif name == "gelu_bf16":
         a = rnd(8192, 8192)
         fn = lambda: ops.gelu(a)
+    elif name == "exp_bf16":
+        a = rnd(8192, 8192)
+        fn = lambda: ops.exp(a)
     elif name == "sum_bf16":
         a = rnd(8192, 8192)
         fn = lambda: ops.sum(a)
+    elif name == "amax_rows_bf16":
+        a = rnd(8192, 8192)
+        fn = lambda: ops.amax(a, [-1])
     elif name == "softmax_bf16":
         a = rnd(32768, 4096)
         fn = lambda: ops.softmax(a, -1)
@@ -575,9 +586,25 @@ def main() -> None:
     p.add_argument("--no-extras", action="store_true", help="skip the op sweep, GEMM set and CPU baseline")
     p.add_argument("--only", default=None,
                    help="run one kernel workload --steps times and exit (for ncu captures)")
+    p.add_argument("--sweep-only", action="store_true",
+                   help="only the memory-bound op sweep (config 2), --steps iterations per kernel")
+    p.add_argument("--gemm-only", action="store_true", help="only the GEMM set (config 3)")
     args = p.parse_args()
     if args.only:
         run_only(args)
+        return
+    if args.gemm_only:
+        import tensorplay_mlu_b200 as tpb
+
+        tpb.load()
+        print(json.dumps({"gemm_set": gemm_set(tpb.ops, peaks()[1])}), flush=True)
+        return
+    if args.sweep_only:
+        import tensorplay_mlu_b200 as tpb
+
+        tpb.load()
+        hbm_peak = peaks()[0]
+        print(json.dumps({"op_sweep": op_sweep(tpb.ops, hbm_peak, iters=args.steps)}), flush=True)
         return
     if args.warmup < 3:
         args.warmup = 3

@@ -170,6 +170,86 @@ template <typename T>
 __device__ __forceinline__ T min_nan(T a, T b) {
     return (a < b || is_nan(a)) ? a : b;
 }
+// fp32: one max.NaN / min.NaN instruction (a NaN operand gives NaN; of two
+// zeros, max gives +0 and min -0 whatever their order).
+template <>
+__device__ __forceinline__ float max_nan<float>(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+template <>
+__device__ __forceinline__ float min_nan<float>(float a, float b) {
+    float r;
+    asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
+// Vector <-> compute-type conversion; 16-bit floats convert in pairs
+// (one packed f32x2 -> bf16x2 / f16x2 instruction per two elements).
+template <typename T, int V, typename C>
+__device__ __forceinline__ void unpack_vec(const Vec<T, V>& v, C (&out)[V]) {
+#pragma unroll
+    for (int j = 0; j < V; ++j) out[j] = load_as<C>(v.v[j]);
+}
+template <int V>
+__device__ __forceinline__ void unpack_vec(const Vec<__nv_bfloat16, V>& v, float (&out)[V]) {
+    if constexpr (V % 2 == 0) {
+#pragma unroll
+        for (int j = 0; j < V; j += 2) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.v[j]));
+            out[j] = f.x;
+            out[j + 1] = f.y;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < V; ++j) out[j] = __bfloat162float(v.v[j]);
+    }
+}
+template <int V>
+__device__ __forceinline__ void unpack_vec(const Vec<__half, V>& v, float (&out)[V]) {
+    if constexpr (V % 2 == 0) {
+#pragma unroll
+        for (int j = 0; j < V; j += 2) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&v.v[j]));
+            out[j] = f.x;
+            out[j + 1] = f.y;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < V; ++j) out[j] = __half2float(v.v[j]);
+    }
+}
+template <typename T, int V, typename C>
+__device__ __forceinline__ void pack_vec(const C (&in)[V], Vec<T, V>& v) {
+#pragma unroll
+    for (int j = 0; j < V; ++j) v.v[j] = store_as<T>(in[j]);
+}
+template <int V>
+__device__ __forceinline__ void pack_vec(const float (&in)[V], Vec<__nv_bfloat16, V>& v) {
+    if constexpr (V % 2 == 0) {
+#pragma unroll
+        for (int j = 0; j < V; j += 2) {
+            *reinterpret_cast<__nv_bfloat162*>(&v.v[j]) = __floats2bfloat162_rn(in[j], in[j + 1]);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < V; ++j) v.v[j] = __float2bfloat16_rn(in[j]);
+    }
+}
+template <int V>
+__device__ __forceinline__ void pack_vec(const float (&in)[V], Vec<__half, V>& v) {
+    if constexpr (V % 2 == 0) {
+#pragma unroll
+        for (int j = 0; j < V; j += 2) {
+            *reinterpret_cast<__half2*>(&v.v[j]) = __floats2half2_rn(in[j], in[j + 1]);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < V; ++j) v.v[j] = __float2half_rn(in[j]);
+    }
+}
+
 
 // Launch helper: number of 256-thread blocks for `work` items of `per_block`.
 inline unsigned blocks_for(int64_t work, int64_t per_block) {

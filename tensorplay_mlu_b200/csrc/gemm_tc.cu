@@ -44,6 +44,7 @@
 #include "common.h"
 #include "device.cuh"
 #include "gemm.h"
+#include "ptx.cuh"
 
 namespace tpb {
 
@@ -54,7 +55,6 @@ namespace {
 constexpr int kThreads = 192;
 constexpr int kBM = 128;
 constexpr int kGroupM = 16;
-constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
 
 // Error codes written to the device error word (role that gave up).
 constexpr int kErrProducer = 0x7c01;
@@ -62,41 +62,6 @@ constexpr int kErrMma = 0x7c02;
 constexpr int kErrEpilogue = 0x7c03;
 
 // ------------------------------------------------------- PTX wrappers --
-
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
 
 // Wait for the phase of parity `parity` to complete.  False when it did not
 // within kWaitNs, or when another role has already given up.
@@ -111,24 +76,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
             return false;
         }
     }
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                            int c0, int c1) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
-        : "memory");
-}
-
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                            int c0, int c1, int c2) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
-        : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -953,10 +900,11 @@ void launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, TcParams& tp, int 
     const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : std::is_same<T, float>::value ? 2u : 0u;
     tp.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (uint32_t(tp.a_mn) << 15) |
                (uint32_t(tp.b_mn) << 16) | (uint32_t(kPairBN >> 3) << 17) | (uint32_t(kPairBM >> 4) << 24);
-    // Row-tile groups sized so the group's A panels (~64 MiB) stay in L2
-    // while B streams past them once.
+    // Row-tile groups sized so the group's A panels (~32 MiB, a quarter of L2:
+    // the two dies each cache their own half) stay resident while B streams
+    // past them.
     const int64_t panel = int64_t(kPairBM) * tp.K * int64_t(sizeof(T));
-    int group_m = static_cast<int>(std::max<int64_t>(1, (int64_t(64) << 20) / std::max<int64_t>(panel, 1)));
+    int group_m = static_cast<int>(std::max<int64_t>(1, (int64_t(32) << 20) / std::max<int64_t>(panel, 1)));
     group_m = std::min(group_m, tp.m_tiles);
     const int clusters = std::min(tp.num_tiles, num_sms(dev) / 2);
     gemm_tc2_kernel<T><<<2 * clusters, kThreads, smem, stream>>>(ma, mb, tp, group_m);
@@ -1073,6 +1021,233 @@ bool gemm_tc_typed(const GemmProblem& p_in, int dev, cudaStream_t stream, CUtens
     return true;
 }
 
+// ---------------------------------------------- fp32 through 3 x TF32 --
+//
+// Without TF32 permission an fp32 product keeps fp32 accuracy by the
+// split-precision ("3xTF32") method: every operand element x is split into
+// hi = tf32(x) and lo = tf32(x - hi), both exact TF32 values (low 13
+// mantissa bits zero, so the tensor core's reading of an fp32 word as TF32
+// changes nothing), and A.B ~= Alo.Bhi + Ahi.Blo + Ahi.Bhi.  The dropped
+// Alo.Blo term and the rounding of lo are both ~2^-22 relative to |a b|.
+// The three products run as TF32 tensor-core GEMMs over K-concatenated
+// operands, K in chunks of kSplitChunk:
+//   A' chunk j = [Alo_j | Ahi_j | Ahi_j],   B' chunk j = [Bhi_j ; Blo_j ; Bhi_j]
+// (both K-major; the small correction terms come first, while the
+// accumulator is still small).  The tensor core adds into its accumulator
+// with truncation after alignment, an error that grows with the number of
+// additions; so each chunk is one GEMM launch whose epilogue adds its
+// result into the output in fp32 with round-to-nearest (beta = 1 after the
+// first chunk), keeping every accumulator chain short.
+// A non-finite element (inf, NaN) has lo = 0, and inf * 0 in a cross term
+// would turn an fp32 inf into NaN; the split marks such rows of A / columns
+// of B and a fix-up pass recomputes the outputs in them with plain fp32 dot
+// products.
+constexpr int64_t kSplitChunk = 1024;
+
+// Round to the nearest TF32 value (ties away from zero); a rounding that
+// would overflow truncates instead; inf and NaN are returned unchanged.
+__device__ __forceinline__ float tf32_round(float x) {
+    const uint32_t u = __float_as_uint(x);
+    if ((u & 0x7f800000u) == 0x7f800000u) return x;
+    uint32_t r = (u + 0x1000u) & 0xffffe000u;
+    if ((r & 0x7f800000u) == 0x7f800000u) r = u & 0xffffe000u;
+    return __uint_as_float(r);
+}
+
+// Rows of a K-major operand (row `row` of batch `row / R` at
+// src + (row / R) * s_b + (row % R) * s_r) into rows of `ld` floats, chunk j
+// of K at j * 3 * kSplitChunk holding its three parts back to back (each
+// K_j = min(kSplitChunk, K - j * kSplitChunk) wide): [lo | hi | hi] for A
+// (b_side 0), [hi | lo | hi] for B (b_side 1).  flags[row] is set when the
+// row holds a non-finite element.
+__global__ void __launch_bounds__(256) split_tf32_kernel(const float* __restrict__ src, float* __restrict__ dst,
+                                                         int64_t rows, int64_t R, int64_t K, int64_t s_b,
+                                                         int64_t s_r, int64_t ld, int b_side,
+                                                         unsigned* __restrict__ flags) {
+    for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+        const float* s = src + (row / R) * s_b + (row % R) * s_r;
+        float* d = dst + row * ld;
+        int bad = 0;
+        for (int64_t k = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; k < K;
+             k += int64_t(gridDim.x) * blockDim.x) {
+            const float x = s[k];
+            const float hi = tf32_round(x);
+            const bool finite = isfinite(x);
+            const float lo = finite ? tf32_round(x - hi) : 0.0f;
+            bad |= !finite;
+            const int64_t j = k / kSplitChunk, kk = k % kSplitChunk;
+            const int64_t kj = K - j * kSplitChunk < kSplitChunk ? K - j * kSplitChunk : kSplitChunk;
+            float* c = d + j * 3 * kSplitChunk + kk;
+            c[0] = b_side ? hi : lo;
+            c[kj] = b_side ? lo : hi;
+            c[2 * kj] = hi;
+        }
+        if (__syncthreads_or(bad) && threadIdx.x == 0) flags[row] = 1u;
+    }
+}
+
+struct FixupParams {
+    const float* a;
+    int64_t sa_b, sa_m, sa_k;
+    const float* b;
+    int64_t sb_b, sb_k, sb_n;
+    float* c;
+    int64_t sc_b, sc_m;
+    const float* cin;
+    int64_t sci_b, sci_m, sci_n;
+    float alpha, beta;
+    int64_t M, N, K, batch;
+    int64_t a_rows_per_batch, b_rows_per_batch;  // 0 when that operand is broadcast over the batch
+};
+
+__device__ __forceinline__ void fixup_one(const FixupParams& p, int64_t bt, int64_t i, int64_t j) {
+    const float* a = p.a + bt * p.sa_b + i * p.sa_m;
+    const float* b = p.b + bt * p.sb_b + j * p.sb_n;
+    float acc = 0.0f;
+    for (int64_t k = 0; k < p.K; ++k) acc = fmaf(a[k * p.sa_k], b[k * p.sb_k], acc);
+    float v = p.alpha * acc;
+    if (p.cin != nullptr) v += p.beta * p.cin[bt * p.sci_b + i * p.sci_m + j * p.sci_n];
+    p.c[bt * p.sc_b + i * p.sc_m + j] = v;
+}
+
+// Block per (batch, row of A) / (batch, column of B): recompute the flagged
+// ones.  Unflagged blocks leave at once.
+__global__ void __launch_bounds__(256) fixup_rows_kernel(FixupParams p, const unsigned* __restrict__ a_flags) {
+    const int64_t bt = blockIdx.y, i = blockIdx.x;
+    if (!a_flags[(p.a_rows_per_batch ? bt : 0) * p.M + i]) return;
+    for (int64_t j = threadIdx.x; j < p.N; j += blockDim.x) fixup_one(p, bt, i, j);
+}
+
+__global__ void __launch_bounds__(256) fixup_cols_kernel(FixupParams p, const unsigned* __restrict__ b_flags) {
+    const int64_t bt = blockIdx.y, j = blockIdx.x;
+    if (!b_flags[(p.b_rows_per_batch ? bt : 0) * p.N + j]) return;
+    for (int64_t i = threadIdx.x; i < p.M; i += blockDim.x) fixup_one(p, bt, i, j);
+}
+
+// A K-major view of an operand: `rows` rows of K floats at base + b*s_b + r*s_r.
+struct KMajor {
+    const float* base;
+    int64_t s_b, s_r;
+};
+
+// Split one operand ([batches, R, K] with strides sb_, sr, sk) into a
+// [batches * R, ld] scratch of split rows; MN-major operands are first
+// copied K-major.
+void split_operand(const float* src, int64_t batches, int64_t R, int64_t K, int64_t s_b, int64_t s_r,
+                   int64_t s_k, int b_side, float* dst, int64_t ld, unsigned* flags,
+                   std::unique_ptr<Scratch>& kmajor, int dev, cudaStream_t stream) {
+    KMajor v{src, s_b, s_r};
+    if (!(s_k == 1 || K == 1)) {
+        kmajor.reset(new Scratch(sizeof(float) * batches * R * K, dev, stream));
+        tpb_tensor s{}, d{};
+        s.data = const_cast<float*>(src);
+        s.dtype = d.dtype = TPB_F32;
+        s.ndim = d.ndim = 3;
+        const int64_t sizes[3] = {batches, R, K};
+        const int64_t sstr[3] = {s_b, s_r, s_k};
+        const int64_t dstr[3] = {R * K, K, 1};
+        for (int i = 0; i < 3; ++i) {
+            s.sizes[i] = d.sizes[i] = sizes[i];
+            s.strides[i] = sstr[i];
+            d.strides[i] = dstr[i];
+        }
+        d.data = kmajor->get();
+        copy_impl(d, s, stream, dev);
+        v = KMajor{static_cast<const float*>(kmajor->get()), R * K, K};
+    }
+    const int64_t rows = batches * R;
+    dim3 grid(static_cast<unsigned>(std::min<int64_t>((K + 255) / 256, 64)),
+              static_cast<unsigned>(std::min<int64_t>(rows, 65535)));
+    split_tf32_kernel<<<grid, 256, 0, stream>>>(v.base, dst, rows, R, K, v.s_b, v.s_r, ld, b_side, flags);
+    check_launch("split_tf32");
+}
+
+// Problems this large take the split path; smaller ones stay on the CUDA
+// cores, where the three-fold operand traffic and launches would not pay.
+bool use_split_tf32(const GemmProblem& p) {
+    static const char* force = std::getenv("TPB200_GEMM_F32");
+    if (force != nullptr && std::strcmp(force, "simt") == 0) return false;
+    if (3 * p.K >= (int64_t(1) << 31) || p.M >= (int64_t(1) << 31) || p.N >= (int64_t(1) << 31)) return false;
+    if (p.batch > 65535) return false;  // the fix-up grids' y extent
+    return p.M >= 128 && p.N >= 128 && p.K >= 16 && p.M * p.N * p.K * p.batch >= (int64_t(1) << 27);
+}
+
+bool gemm_f32_split(const GemmProblem& p, int dev, cudaStream_t stream) {
+    if (!use_split_tf32(p)) return false;
+    const int64_t chunks = (p.K + kSplitChunk - 1) / kSplitChunk;
+    const int64_t ld = chunks * 3 * kSplitChunk;  // a multiple of 4: 16-byte row pitch
+    const int64_t a_batches = p.sa_b == 0 ? 1 : p.batch;
+    const int64_t b_batches = p.sb_b == 0 ? 1 : p.batch;
+    Scratch a3(sizeof(float) * a_batches * p.M * ld, dev, stream);
+    Scratch b3(sizeof(float) * b_batches * p.N * ld, dev, stream);
+    const int64_t nflags = a_batches * p.M + b_batches * p.N;
+    Scratch flags(sizeof(unsigned) * nflags, dev, stream);
+    TPB_CUDA(cudaMemsetAsync(flags.get(), 0, sizeof(unsigned) * nflags, stream));
+    unsigned* a_flags = static_cast<unsigned*>(flags.get());
+    unsigned* b_flags = a_flags + a_batches * p.M;
+    std::unique_ptr<Scratch> a_k, b_k;
+    split_operand(static_cast<const float*>(p.a), a_batches, p.M, p.K, p.sa_b, p.sa_m, p.sa_k, 0,
+                  static_cast<float*>(a3.get()), ld, a_flags, a_k, dev, stream);
+    split_operand(static_cast<const float*>(p.b), b_batches, p.N, p.K, p.sb_b, p.sb_n, p.sb_k, 1,
+                  static_cast<float*>(b3.get()), ld, b_flags, b_k, dev, stream);
+    a_k.reset();
+    b_k.reset();
+    for (int64_t j = 0; j < chunks; ++j) {
+        const int64_t kj = std::min(kSplitChunk, p.K - j * kSplitChunk);
+        GemmProblem q = p;
+        q.K = 3 * kj;
+        q.a = static_cast<const float*>(a3.get()) + j * 3 * kSplitChunk;
+        q.sa_k = 1;
+        q.sa_m = ld;
+        q.sa_b = a_batches > 1 ? p.M * ld : 0;
+        q.b = static_cast<const float*>(b3.get()) + j * 3 * kSplitChunk;
+        q.sb_k = 1;
+        q.sb_n = ld;
+        q.sb_b = b_batches > 1 ? p.N * ld : 0;
+        q.flags = p.flags | TPB_GEMM_ALLOW_TF32;
+        if (j > 0) {  // out = alpha * A_j.B_j + out
+            q.cin = p.c;
+            q.sci_b = p.sc_b;
+            q.sci_m = p.sc_m;
+            q.sci_n = 1;
+            q.beta = 1.0;
+        }
+        TPB_CHECK(gemm_tc_typed<float>(q, dev, stream, CU_TENSOR_MAP_DATA_TYPE_FLOAT32),
+                  "gemm: the split-TF32 operands were not accepted by the tensor-core kernel");
+    }
+    FixupParams f{};
+    f.a = static_cast<const float*>(p.a);
+    f.sa_b = p.sa_b;
+    f.sa_m = p.sa_m;
+    f.sa_k = p.sa_k;
+    f.b = static_cast<const float*>(p.b);
+    f.sb_b = p.sb_b;
+    f.sb_k = p.sb_k;
+    f.sb_n = p.sb_n;
+    f.c = static_cast<float*>(p.c);
+    f.sc_b = p.sc_b;
+    f.sc_m = p.sc_m;
+    f.cin = static_cast<const float*>(p.cin);
+    f.sci_b = p.sci_b;
+    f.sci_m = p.sci_m;
+    f.sci_n = p.sci_n;
+    f.alpha = static_cast<float>(p.alpha);
+    f.beta = static_cast<float>(p.beta);
+    f.M = p.M;
+    f.N = p.N;
+    f.K = p.K;
+    f.batch = p.batch;
+    f.a_rows_per_batch = a_batches > 1 ? p.M : 0;
+    f.b_rows_per_batch = b_batches > 1 ? p.N : 0;
+    fixup_rows_kernel<<<dim3(static_cast<unsigned>(p.M), static_cast<unsigned>(p.batch)), 256, 0, stream>>>(
+        f, a_flags);
+    check_launch("gemm_f32_fixup_rows");
+    fixup_cols_kernel<<<dim3(static_cast<unsigned>(p.N), static_cast<unsigned>(p.batch)), 256, 0, stream>>>(
+        f, b_flags);
+    check_launch("gemm_f32_fixup_cols");
+    return true;
+}
+
 }  // namespace
 
 bool gemm_tc(const GemmProblem& p, int dev, cudaStream_t stream) {
@@ -1081,7 +1256,7 @@ bool gemm_tc(const GemmProblem& p, int dev, cudaStream_t stream) {
         case TPB_BF16: return gemm_tc_typed<__nv_bfloat16>(p, dev, stream, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
         case TPB_F16: return gemm_tc_typed<__half>(p, dev, stream, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
         case TPB_F32:
-            if (!(p.flags & TPB_GEMM_ALLOW_TF32)) return false;
+            if (!(p.flags & TPB_GEMM_ALLOW_TF32)) return gemm_f32_split(p, dev, stream);
             return gemm_tc_typed<float>(p, dev, stream, CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
         default: return false;
     }

@@ -5,6 +5,7 @@
 // Reductions: the input's dimensions are split into kept and reduced ones and
 // each group is coalesced.  Three kernels cover the layouts:
 //   * rows: the reduced elements of one output are contiguous ([.., R]);
+//     many rows take one warp each (grid-stride over rows); fewer rows take
 //     one block per (row, split), 16-byte vector loads, warp-shuffle then
 //     shared-memory block reduction;
 //   * columns: the output index is the contiguous side ([O, R, K] over R);
@@ -17,19 +18,34 @@
 //
 // Softmax: rows of up to 8192 (fp32) / 16384 (16-bit) elements stay in
 // registers between the max, the sum and the write -- one read and one write
-// of HBM; longer rows use an online max/sum pass plus a write pass, and
-// softmax over a non-innermost dimension walks columns.
+// of HBM.  With many such rows a persistent block streams them through a ring
+// of shared-memory stages filled by bulk asynchronous copies (TMA), so the
+// next rows' reads overlap the current row's reductions.  Longer rows use an
+// online max/sum pass plus a write pass, and softmax over a non-innermost
+// dimension walks columns.
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <cfloat>
 #include <climits>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <utility>
 #include <mutex>
 #include <type_traits>
 
 #include "common.h"
 #include "device.cuh"
+#include "ptx.cuh"
+
+// Completion tickets of single-row split reductions, one per (device,
+// stream): the blocks of a launch count themselves in, the last one combines
+// the partial results and resets its ticket to zero for the stream's next
+// reduction (launches on one stream never overlap).
+constexpr int kTicketSlots = 256;
+static __device__ unsigned g_reduce_tickets[kTicketSlots];
 
 namespace tpb {
 
@@ -117,12 +133,17 @@ __device__ __forceinline__ To finalize(A v, double count) {
 // -------------------------------------------------------- row reduce --
 
 // rows x R, row r starting at x + row_off(r), elements contiguous.  Block b
-// handles row b / splits, chunk b % splits.
+// handles row b / splits as split b % splits: the row's 16-byte vectors are
+// dealt out in an interleaved (grid-stride) order -- split s takes vectors
+// s * kThreads + t, + splits * kThreads, ... -- so at any moment the blocks
+// of a row sweep neighbouring memory, and every split gets the same share to
+// within one vector per thread.  Split 0 also takes the scalar head (before
+// the first 16-byte boundary) and tail.
 template <typename T, typename To, int OP>
 __global__ void __launch_bounds__(kThreads) reduce_rows(const T* __restrict__ x, To* __restrict__ out,
                                                         typename Acc<T>::type* __restrict__ partial,
                                                         OffsetCalc<1> rows_calc, int64_t R, int splits,
-                                                        int64_t chunk, double count) {
+                                                        double count, unsigned* __restrict__ ticket) {
     using A = typename Acc<T>::type;
     constexpr int V = VecWidth<T>::value;
     using VT = Vec<T, V>;
@@ -131,42 +152,235 @@ __global__ void __launch_bounds__(kThreads) reduce_rows(const T* __restrict__ x,
     int64_t off;
     rows_calc.get(static_cast<uint32_t>(row), &off);
     const T* base = x + off;
-    const int64_t begin = int64_t(split) * chunk;
-    const int64_t end = begin + chunk < R ? begin + chunk : R;
-    A acc0 = identity<A, OP>(), acc1 = identity<A, OP>();
-    int64_t i = begin;
-    // Scalar head until the pointer is 16-byte aligned, then vectors.
-    while (i < end && !aligned16(base + i) && (i - begin) < V) {
-        if (threadIdx.x == 0) acc0 = combine<A, OP>(acc0, load_as<A>(base[i]));
-        ++i;
+    A acc0 = identity<A, OP>(), acc1 = identity<A, OP>(), acc2 = identity<A, OP>(),
+      acc3 = identity<A, OP>();
+    const int64_t mis = static_cast<int64_t>(reinterpret_cast<uintptr_t>(base) & 15u);
+    int64_t head = mis == 0 ? 0 : (16 - mis) / static_cast<int64_t>(sizeof(T));
+    if (head > R) head = R;
+    if (split == 0 && threadIdx.x < head) acc0 = combine<A, OP>(acc0, load_as<A>(base[threadIdx.x]));
+    const int64_t nvec = (R - head) / V;
+    const VT* vp = reinterpret_cast<const VT*>(base + head);
+    // Four 16-byte loads in flight per thread.
+    const int64_t S = int64_t(splits) * kThreads;
+    int64_t v = int64_t(split) * kThreads + threadIdx.x;
+    for (; v + 3 * S < nvec; v += 4 * S) {
+        const VT a = vp[v];
+        const VT b = vp[v + S];
+        const VT c = vp[v + 2 * S];
+        const VT d = vp[v + 3 * S];
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            acc0 = combine<A, OP>(acc0, load_as<A>(a.v[j]));
+            acc1 = combine<A, OP>(acc1, load_as<A>(b.v[j]));
+            acc2 = combine<A, OP>(acc2, load_as<A>(c.v[j]));
+            acc3 = combine<A, OP>(acc3, load_as<A>(d.v[j]));
+        }
     }
-    if (aligned16(base + i)) {
-        const int64_t nvec = (end - i) / V;
-        const VT* vp = reinterpret_cast<const VT*>(base + i);
-        int64_t v = threadIdx.x;
-        for (; v + kThreads < nvec; v += 2 * kThreads) {
+    for (; v < nvec; v += S) {
+        const VT a = vp[v];
+#pragma unroll
+        for (int j = 0; j < V; ++j) acc0 = combine<A, OP>(acc0, load_as<A>(a.v[j]));
+    }
+    if (split == 0) {
+        for (int64_t k = head + nvec * V + threadIdx.x; k < R; k += kThreads) {
+            acc1 = combine<A, OP>(acc1, load_as<A>(base[k]));
+        }
+    }
+    A acc = block_combine<A, OP>(combine<A, OP>(combine<A, OP>(acc0, acc1), combine<A, OP>(acc2, acc3)));
+    if (threadIdx.x == 0) {
+        if (splits == 1) out[row] = finalize<To, A, OP>(acc, count);
+        else partial[row * splits + split] = acc;
+    }
+    if (ticket == nullptr) return;
+    // One row split over the grid: the last block to finish combines the
+    // partials, in the same order as reduce_row_partials (so the result does
+    // not depend on which block is last).
+    __shared__ bool last;
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(ticket, 1u) == static_cast<unsigned>(splits - 1);
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    A a = identity<A, OP>();
+    for (int s = threadIdx.x; s < splits; s += kThreads) a = combine<A, OP>(a, __ldcg(partial + s));
+    a = block_combine<A, OP>(a);
+    if (threadIdx.x == 0) {
+        out[0] = finalize<To, A, OP>(a, count);
+        *ticket = 0u;
+    }
+}
+
+// Many rows, none split: one warp per row, rows taken in a grid-stride loop,
+// so an SM streams rows back to back with no block-wide barrier between them
+// (a block per short row spends most of its life in launch, barriers and
+// teardown).  Four 16-byte loads in flight per lane.
+constexpr int kWarpsPerBlock = kThreads / 32;
+
+template <typename T, typename To, int OP>
+__global__ void __launch_bounds__(kThreads) reduce_rows_warp(const T* __restrict__ x, To* __restrict__ out,
+                                                             OffsetCalc<1> rows_calc, int64_t rows,
+                                                             int64_t R, double count) {
+    using A = typename Acc<T>::type;
+    constexpr int V = VecWidth<T>::value;
+    using VT = Vec<T, V>;
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = int64_t(gridDim.x) * kWarpsPerBlock;
+    for (int64_t row = int64_t(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5); row < rows; row += nwarps) {
+        int64_t off;
+        rows_calc.get(static_cast<uint32_t>(row), &off);
+        const T* base = x + off;
+        A acc0 = identity<A, OP>(), acc1 = identity<A, OP>(), acc2 = identity<A, OP>(),
+          acc3 = identity<A, OP>();
+        // Elements before the first 16-byte boundary (fewer than V).
+        const int64_t mis = static_cast<int64_t>(reinterpret_cast<uintptr_t>(base) & 15u);
+        int64_t head = mis == 0 ? 0 : (16 - mis) / static_cast<int64_t>(sizeof(T));
+        if (head > R) head = R;
+        if (lane < head) acc0 = combine<A, OP>(acc0, load_as<A>(base[lane]));
+        const int64_t nvec = (R - head) / V;
+        const VT* vp = reinterpret_cast<const VT*>(base + head);
+        int64_t v = lane;
+        for (; v + 96 < nvec; v += 128) {
             const VT a = vp[v];
-            const VT b = vp[v + kThreads];
+            const VT b = vp[v + 32];
+            const VT c = vp[v + 64];
+            const VT d = vp[v + 96];
 #pragma unroll
             for (int j = 0; j < V; ++j) {
                 acc0 = combine<A, OP>(acc0, load_as<A>(a.v[j]));
                 acc1 = combine<A, OP>(acc1, load_as<A>(b.v[j]));
+                acc2 = combine<A, OP>(acc2, load_as<A>(c.v[j]));
+                acc3 = combine<A, OP>(acc3, load_as<A>(d.v[j]));
+            }
+        }
+        for (; v < nvec; v += 32) {
+            const VT a = vp[v];
+#pragma unroll
+            for (int j = 0; j < V; ++j) acc1 = combine<A, OP>(acc1, load_as<A>(a.v[j]));
+        }
+        for (int64_t k = head + nvec * V + lane; k < R; k += 32) {
+            acc2 = combine<A, OP>(acc2, load_as<A>(base[k]));
+        }
+        const A acc = warp_combine<A, OP>(combine<A, OP>(combine<A, OP>(acc0, acc1), combine<A, OP>(acc2, acc3)));
+        if (lane == 0) out[row] = finalize<To, A, OP>(acc, count);
+    }
+}
+
+// Rows streamed through shared memory: work items are (row, chunk of
+// kChunkBytes), a persistent block takes items blockIdx.x, +gridDim.x, ...
+// with kReduceStages of them in flight as bulk asynchronous copies (TMA), so
+// reads continue while the block combines.  A row of one chunk is written
+// to `out`; longer rows leave one partial per chunk for the second pass.
+// Rows start on 16-byte boundaries; a chunk's last (< 16) bytes are read
+// from global memory directly.  Waits are bounded as in the softmax ring.
+constexpr uint32_t kChunkBytes = 16384;
+constexpr int kReduceStages = 4;
+constexpr int kErrReduceRing = 0x7c12;
+
+template <typename T>
+__device__ __forceinline__ void issue_chunk(const T* x, int64_t item, int64_t n_chunks, int64_t R,
+                                            int64_t row_stride, int64_t chunk, uint32_t dst, uint32_t bar) {
+    const int64_t row = item / n_chunks, c = item % n_chunks;
+    const int64_t e0 = c * chunk;
+    const int64_t n = R - e0 < chunk ? R - e0 : chunk;
+    const uint32_t bytes = static_cast<uint32_t>(n * int64_t(sizeof(T))) & ~15u;
+    if (bytes != 0) {
+        mbar_expect_tx(bar, bytes);
+        bulk_load(dst, x + row * row_stride + e0, bytes, bar);
+    } else {
+        mbar_arrive(bar);  // nothing to copy: complete the phase
+    }
+}
+
+template <typename T, typename To, int OP>
+__global__ void __launch_bounds__(kThreads) reduce_rows_ring(const T* __restrict__ x, To* __restrict__ out,
+                                                             typename Acc<T>::type* __restrict__ partial,
+                                                             int64_t rows, int64_t R, int64_t row_stride,
+                                                             int64_t chunk, int64_t n_chunks, double count,
+                                                             int* err) {
+    using A = typename Acc<T>::type;
+    constexpr int V = VecWidth<T>::value;
+    using VT = Vec<T, V>;
+    extern __shared__ __align__(128) unsigned char ring[];
+    __shared__ __align__(8) uint64_t full[kReduceStages];
+    __shared__ volatile int gave_up;
+    const int64_t items = rows * n_chunks;
+    const int64_t first = blockIdx.x, stride = gridDim.x;
+    if (threadIdx.x == 0) {
+        gave_up = 0;
+        for (int s = 0; s < kReduceStages; ++s) mbar_init(smem_addr(&full[s]), 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kReduceStages; ++s) {
+            const int64_t item = first + int64_t(s) * stride;
+            if (item >= items) break;
+            issue_chunk(x, item, n_chunks, R, row_stride, chunk, smem_addr(ring + size_t(s) * kChunkBytes),
+                        smem_addr(&full[s]));
+        }
+    }
+    int it = 0, s = 0;
+    uint32_t parity = 0;
+    for (int64_t item = first; item < items; item += stride, ++it) {
+        if (!mbar_wait_bounded(smem_addr(&full[s]), parity)) {
+            gave_up = 1;
+            atomicExch(err, kErrReduceRing);
+        }
+        const int64_t row = item / n_chunks, c = item % n_chunks;
+        const int64_t e0 = c * chunk;
+        const int64_t n = R - e0 < chunk ? R - e0 : chunk;
+        const int64_t nvec = (n * int64_t(sizeof(T)) / 16);
+        const VT* sv = reinterpret_cast<const VT*>(ring + size_t(s) * kChunkBytes);
+        A acc0 = identity<A, OP>(), acc1 = identity<A, OP>(), acc2 = identity<A, OP>(),
+          acc3 = identity<A, OP>();
+        int64_t v = threadIdx.x;
+        for (; v + 3 * kThreads < nvec; v += 4 * kThreads) {
+            const VT a = sv[v];
+            const VT b = sv[v + kThreads];
+            const VT cc = sv[v + 2 * kThreads];
+            const VT d = sv[v + 3 * kThreads];
+#pragma unroll
+            for (int j = 0; j < V; ++j) {
+                acc0 = combine<A, OP>(acc0, load_as<A>(a.v[j]));
+                acc1 = combine<A, OP>(acc1, load_as<A>(b.v[j]));
+                acc2 = combine<A, OP>(acc2, load_as<A>(cc.v[j]));
+                acc3 = combine<A, OP>(acc3, load_as<A>(d.v[j]));
             }
         }
         for (; v < nvec; v += kThreads) {
-            const VT a = vp[v];
+            const VT a = sv[v];
 #pragma unroll
             for (int j = 0; j < V; ++j) acc0 = combine<A, OP>(acc0, load_as<A>(a.v[j]));
         }
-        i += nvec * V;
+        const T* g = x + row * row_stride + e0;
+        for (int64_t k = nvec * V + threadIdx.x; k < n; k += kThreads) {
+            acc1 = combine<A, OP>(acc1, load_as<A>(g[k]));
+        }
+        const A acc = block_combine<A, OP>(combine<A, OP>(combine<A, OP>(acc0, acc1), combine<A, OP>(acc2, acc3)));
+        // Every thread has read stage s (block_combine's barriers): refill it.
+        if (threadIdx.x == 0) {
+            const int64_t next = item + int64_t(kReduceStages) * stride;
+            if (next < items && !gave_up) {
+                issue_chunk(x, next, n_chunks, R, row_stride, chunk, smem_addr(ring + size_t(s) * kChunkBytes),
+                            smem_addr(&full[s]));
+            }
+            if (n_chunks == 1) out[row] = finalize<To, A, OP>(acc, count);
+            else partial[item] = acc;
+        }
+        if (gave_up) break;
+        if (++s == kReduceStages) {
+            s = 0;
+            parity ^= 1u;
+        }
     }
-    for (int64_t k = i + threadIdx.x; k < end; k += kThreads) {
-        acc1 = combine<A, OP>(acc1, load_as<A>(base[k]));
-    }
-    A acc = block_combine<A, OP>(combine<A, OP>(acc0, acc1));
-    if (threadIdx.x == 0) {
-        if (splits == 1) out[row] = finalize<To, A, OP>(acc, count);
-        else partial[row * splits + split] = acc;
+    if (threadIdx.x == 0 && gave_up) {
+        for (int k = 0; k < kReduceStages; ++k) {
+            const int j = it + k;
+            if (first + int64_t(j) * stride >= items) break;
+            mbar_wait_bounded(smem_addr(&full[j % kReduceStages]), static_cast<uint32_t>(j / kReduceStages) & 1u);
+        }
     }
 }
 
@@ -187,12 +401,14 @@ __global__ void __launch_bounds__(kThreads) reduce_row_partials(const A* __restr
 // ----------------------------------------------------- column reduce --
 
 // x viewed as [O, R, K]: offset o*os + r*rs + k (k contiguous).  Grid:
-// (ceil(K / (V*threads)), O, splits).
+// (ceil(K / (V*threads)), O, splits).  Split s walks rows s, s + splits, ...
+// (neighbouring splits read neighbouring rows), four rows in flight in two
+// accumulator chains.
 template <typename T, typename To, int OP, int V>
 __global__ void __launch_bounds__(kThreads) reduce_cols(const T* __restrict__ x, To* __restrict__ out,
                                                         typename Acc<T>::type* __restrict__ partial,
                                                         int64_t O, int64_t R, int64_t K, int64_t os,
-                                                        int64_t rs, int64_t rchunk, double count) {
+                                                        int64_t rs, double count) {
     using A = typename Acc<T>::type;
     using VT = Vec<T, V>;
     const int64_t kv = int64_t(blockIdx.x) * kThreads + threadIdx.x;
@@ -200,27 +416,33 @@ __global__ void __launch_bounds__(kThreads) reduce_cols(const T* __restrict__ x,
     const int64_t o = blockIdx.y;
     const int split = blockIdx.z;
     const int splits = gridDim.z;
-    const int64_t r0 = int64_t(split) * rchunk;
-    const int64_t r1 = r0 + rchunk < R ? r0 + rchunk : R;
-    A acc[V];
+    A acc[V], acc2[V];
 #pragma unroll
-    for (int j = 0; j < V; ++j) acc[j] = identity<A, OP>();
+    for (int j = 0; j < V; ++j) acc[j] = acc2[j] = identity<A, OP>();
     const T* p = x + o * os + kv * V;
-    int64_t r = r0;
-    for (; r + 1 < r1; r += 2) {
-        const VT a = *reinterpret_cast<const VT*>(p + r * rs);
-        const VT b = *reinterpret_cast<const VT*>(p + (r + 1) * rs);
+    const int64_t step = int64_t(splits) * rs;
+    int64_t r = split;
+    for (; r + 3 * int64_t(splits) < R; r += 4 * int64_t(splits)) {
+        const T* q = p + r * rs;
+        const VT a = *reinterpret_cast<const VT*>(q);
+        const VT b = *reinterpret_cast<const VT*>(q + step);
+        const VT c = *reinterpret_cast<const VT*>(q + 2 * step);
+        const VT d = *reinterpret_cast<const VT*>(q + 3 * step);
 #pragma unroll
         for (int j = 0; j < V; ++j) {
             acc[j] = combine<A, OP>(acc[j], load_as<A>(a.v[j]));
-            acc[j] = combine<A, OP>(acc[j], load_as<A>(b.v[j]));
+            acc2[j] = combine<A, OP>(acc2[j], load_as<A>(b.v[j]));
+            acc[j] = combine<A, OP>(acc[j], load_as<A>(c.v[j]));
+            acc2[j] = combine<A, OP>(acc2[j], load_as<A>(d.v[j]));
         }
     }
-    if (r < r1) {
+    for (; r < R; r += splits) {
         const VT a = *reinterpret_cast<const VT*>(p + r * rs);
 #pragma unroll
         for (int j = 0; j < V; ++j) acc[j] = combine<A, OP>(acc[j], load_as<A>(a.v[j]));
     }
+#pragma unroll
+    for (int j = 0; j < V; ++j) acc[j] = combine<A, OP>(acc[j], acc2[j]);
     if (splits == 1) {
 #pragma unroll
         for (int j = 0; j < V; ++j) out[o * K + kv * V + j] = finalize<To, A, OP>(acc[j], count);
@@ -235,24 +457,46 @@ template <typename A, typename To, int OP>
 __global__ void __launch_bounds__(kThreads) reduce_col_partials(const A* __restrict__ partial,
                                                                 To* __restrict__ out, int64_t n,
                                                                 int splits, double count) {
-    for (int64_t i = int64_t(blockIdx.x) * kThreads + threadIdx.x; i < n;
-         i += int64_t(gridDim.x) * kThreads) {
-        A acc = identity<A, OP>();
-        for (int s = 0; s < splits; ++s) acc = combine<A, OP>(acc, partial[int64_t(s) * n + i]);
+    // Block = 32 columns x 8 split lanes: lane y combines splits y, y+8, ...
+    // (two independent chains), then lane 0 combines the 8 lane results in
+    // order -- a fixed order, so results are deterministic.
+    __shared__ A lanes[8][33];
+    const int x = threadIdx.x & 31, y = threadIdx.x >> 5;
+    const int64_t i = int64_t(blockIdx.x) * 32 + x;
+    A a0 = identity<A, OP>(), a1 = identity<A, OP>();
+    if (i < n) {
+        int s = y;
+        for (; s + 8 < splits; s += 16) {
+            a0 = combine<A, OP>(a0, partial[int64_t(s) * n + i]);
+            a1 = combine<A, OP>(a1, partial[int64_t(s + 8) * n + i]);
+        }
+        if (s < splits) a0 = combine<A, OP>(a0, partial[int64_t(s) * n + i]);
+    }
+    lanes[y][x] = combine<A, OP>(a0, a1);
+    __syncthreads();
+    if (y == 0 && i < n) {
+        A acc = lanes[0][x];
+#pragma unroll
+        for (int k = 1; k < 8; ++k) acc = combine<A, OP>(acc, lanes[k][x]);
         out[i] = finalize<To, A, OP>(acc, count);
     }
 }
 
 // ------------------------------------------------------------- softmax --
 
-template <typename C>
+// exp / log of the softmax family.  16-bit outputs (rounded to 8 or 11
+// mantissa bits) use the hardware ex2/lg2 approximations; fp32 / fp64 the
+// accurate functions.
+template <typename T, typename C>
 __device__ __forceinline__ C sm_exp(C x) {
     if constexpr (std::is_same<C, double>::value) return exp(x);
+    else if constexpr (sizeof(T) == 2) return __expf(x);
     else return expf(x);
 }
-template <typename C>
+template <typename T, typename C>
 __device__ __forceinline__ C sm_log(C x) {
     if constexpr (std::is_same<C, double>::value) return log(x);
+    else if constexpr (sizeof(T) == 2) return __logf(x);
     else return logf(x);
 }
 
@@ -271,55 +515,161 @@ __device__ __forceinline__ C block_bcast(C v) {
     return slot;
 }
 
-// One block per row of D elements kept in registers: VPT vectors of V
-// elements per thread (V = 1 when the row is not vector-aligned).
-template <typename T, int V, int VPT, int THREADS>
-__global__ void __launch_bounds__(THREADS) softmax_rows_reg(const T* __restrict__ x, T* __restrict__ y,
-                                                            int64_t D, bool log) {
+// exp(v - m).  For 16-bit outputs: one FFMA and one ex2.approx on
+// v * log2(e) - m * log2(e) (ml2 = m * log2(e), computed once per row).
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+template <typename T, typename C>
+__device__ __forceinline__ C sm_exp_shift(C v, C m, C ml2) {
+    if constexpr (sizeof(T) == 2) return ex2_approx(fmaf(v, kLog2e, -ml2));
+    else return sm_exp<T>(v - m);
+}
+
+// Softmax of one row of D elements held by the block: VPT vectors of V
+// elements per thread stay in registers between the max, the sum and the
+// write.  `after_read()` runs once every thread has read its elements (the
+// first block reduction's barriers have passed).
+template <typename T, int V, int VPT, int THREADS, bool LOG, typename AfterRead>
+__device__ __forceinline__ void softmax_row(const T* __restrict__ xr, T* __restrict__ yr, int64_t D,
+                                            AfterRead after_read) {
     using C = typename Compute<T>::type;
     using VT = Vec<T, V>;
-    const int64_t row = blockIdx.x;
-    const T* xr = x + row * D;
-    T* yr = y + row * D;
     C v[VPT][V];
     C m = -INFINITY;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
         const int64_t idx = (int64_t(k) * THREADS + threadIdx.x) * V;
         if (idx < D) {
-            const VT a = *reinterpret_cast<const VT*>(xr + idx);
+            unpack_vec(*reinterpret_cast<const VT*>(xr + idx), v[k]);
 #pragma unroll
-            for (int j = 0; j < V; ++j) {
-                v[k][j] = load_as<C>(a.v[j]);
-                m = max_nan(m, v[k][j]);
-            }
+            for (int j = 0; j < V; ++j) m = max_nan(m, v[k][j]);
         } else {
 #pragma unroll
             for (int j = 0; j < V; ++j) v[k][j] = -INFINITY;
         }
     }
     m = block_bcast(block_max(m));
+    after_read();
+    const C ml2 = m * C(kLog2e);
     C s = 0;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
 #pragma unroll
         for (int j = 0; j < V; ++j) {
-            const C e = sm_exp(v[k][j] - m);
+            const C e = sm_exp_shift<T>(v[k][j], m, ml2);
             s += e;
-            if (!log) v[k][j] = e;
+            if constexpr (!LOG) v[k][j] = e;
         }
     }
     s = block_bcast(block_sum(s));
-    const C inv = C(1) / s;
-    const C lse = sm_log(s);
+    if constexpr (LOG) {
+        // (v - m) - log(s): two roundings of small numbers, not one of m + log(s).
+        const C lse = sm_log<T>(s);
+#pragma unroll
+        for (int k = 0; k < VPT; ++k)
+#pragma unroll
+            for (int j = 0; j < V; ++j) v[k][j] = (v[k][j] - m) - lse;
+    } else {
+        const C inv = C(1) / s;
+#pragma unroll
+        for (int k = 0; k < VPT; ++k)
+#pragma unroll
+            for (int j = 0; j < V; ++j) v[k][j] *= inv;
+    }
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
         const int64_t idx = (int64_t(k) * THREADS + threadIdx.x) * V;
         if (idx < D) {
             VT o;
-#pragma unroll
-            for (int j = 0; j < V; ++j) o.v[j] = store_as<T>(log ? v[k][j] - m - lse : v[k][j] * inv);
+            pack_vec(v[k], o);
             *reinterpret_cast<VT*>(yr + idx) = o;
+        }
+    }
+}
+
+// One block per row (V = 1 when the row is not vector-aligned).
+template <typename T, int V, int VPT, int THREADS, bool LOG>
+__global__ void __launch_bounds__(THREADS) softmax_rows_reg(const T* __restrict__ x, T* __restrict__ y,
+                                                            int64_t D) {
+    const int64_t row = blockIdx.x;
+    softmax_row<T, V, VPT, THREADS, LOG>(x + row * D, y + row * D, D, [] {});
+}
+
+// Many rows that fit in registers: a persistent block walks rows
+// blockIdx.x, +gridDim.x, ... with `stages` of them in flight as bulk copies
+// into shared memory (one mbarrier per stage), so HBM reads continue while
+// the block's max / sum / write of the current row run.  Thread 0 refills a
+// stage as soon as the first block reduction shows every thread has read it.
+// A wait that gives up (kWaitNs) records kErrSoftmaxRing in the device error
+// word; the block then finishes the row it is on, drains the copies it issued
+// and returns.
+constexpr int kMaxRingStages = 8;
+constexpr int kErrSoftmaxRing = 0x7c11;
+
+template <typename T, int V, int VPT, int THREADS, bool LOG>
+__global__ void __launch_bounds__(THREADS) softmax_rows_ring(const T* __restrict__ x, T* __restrict__ y,
+                                                             int64_t rows, int64_t D, int stages, int* err) {
+    extern __shared__ __align__(128) unsigned char ring[];
+    __shared__ __align__(8) uint64_t full[kMaxRingStages];
+    __shared__ volatile int gave_up;
+    const uint32_t row_bytes = static_cast<uint32_t>(D * sizeof(T));
+    const uint32_t stage_bytes = (row_bytes + 127u) & ~127u;
+    const int64_t first = blockIdx.x, stride = gridDim.x;
+    if (threadIdx.x == 0) {
+        gave_up = 0;
+        for (int s = 0; s < stages; ++s) mbar_init(smem_addr(&full[s]), 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            const int64_t r = first + int64_t(s) * stride;
+            if (r >= rows) break;
+            mbar_expect_tx(smem_addr(&full[s]), row_bytes);
+            bulk_load(smem_addr(ring + size_t(s) * stage_bytes), x + r * D, row_bytes, smem_addr(&full[s]));
+        }
+    }
+    int it = 0;
+    int s = 0;
+    uint32_t parity = 0;
+    for (int64_t r = first; r < rows; r += stride, ++it) {
+        if (!mbar_wait_bounded(smem_addr(&full[s]), parity)) {
+            gave_up = 1;
+            atomicExch(err, kErrSoftmaxRing);
+        }
+        const T* xs = reinterpret_cast<const T*>(ring + size_t(s) * stage_bytes);
+        const int64_t next = r + int64_t(stages) * stride;
+        const int stage = s;
+        softmax_row<T, V, VPT, THREADS, LOG>(xs, y + r * D, D, [&] {
+            // Every thread has read stage `stage`: refill it.
+            if (threadIdx.x == 0 && next < rows && !gave_up) {
+                mbar_expect_tx(smem_addr(&full[stage]), row_bytes);
+                bulk_load(smem_addr(ring + size_t(stage) * stage_bytes), x + next * D, row_bytes,
+                          smem_addr(&full[stage]));
+            }
+        });
+        // gave_up was set before the block reductions' barriers: uniform.
+        if (gave_up) break;
+        if (++s == stages) {
+            s = 0;
+            parity ^= 1u;
+        }
+    }
+    // After giving up, wait (bounded) for the copies still in flight so none
+    // lands in shared memory after the block has left.  Those are the
+    // iterations it .. it + stages - 1 (the refill of iteration it was
+    // skipped).
+    if (threadIdx.x == 0 && gave_up) {
+        for (int k = 0; k < stages; ++k) {
+            const int j = it + k;
+            if (first + int64_t(j) * stride >= rows) break;
+            mbar_wait_bounded(smem_addr(&full[j % stages]), static_cast<uint32_t>(j / stages) & 1u);
         }
     }
 }
@@ -336,21 +686,21 @@ __global__ void __launch_bounds__(kThreads) softmax_rows_online(const T* __restr
     for (int64_t i = threadIdx.x; i < D; i += kThreads) {
         const C v = load_as<C>(xr[i]);
         if (v > m) {
-            s = s * sm_exp(m - v) + C(1);
+            s = s * sm_exp<T>(m - v) + C(1);
             m = v;
         } else if (v != v) {
             m = v;
         } else {
-            s += sm_exp(v - m);
+            s += sm_exp<T>(v - m);
         }
     }
     const C gm = block_bcast(block_max(m));
-    s = (m == -INFINITY) ? C(0) : s * sm_exp(m - gm);
+    s = (m == -INFINITY) ? C(0) : s * sm_exp<T>(m - gm);
     s = block_bcast(block_sum(s));
-    const C inv = C(1) / s, lse = sm_log(s);
+    const C inv = C(1) / s, lse = sm_log<T>(s);
     for (int64_t i = threadIdx.x; i < D; i += kThreads) {
         const C v = load_as<C>(xr[i]);
-        yr[i] = store_as<T>(log ? v - gm - lse : sm_exp(v - gm) * inv);
+        yr[i] = store_as<T>(log ? v - gm - lse : sm_exp<T>(v - gm) * inv);
     }
 }
 
@@ -370,18 +720,18 @@ __global__ void __launch_bounds__(kThreads) softmax_cols(const T* __restrict__ x
         for (int64_t d = 0; d < D; ++d) {
             const C v = load_as<C>(xc[d * inner]);
             if (v > m) {
-                s = s * sm_exp(m - v) + C(1);
+                s = s * sm_exp<T>(m - v) + C(1);
                 m = v;
             } else if (v != v) {
                 m = v;
             } else {
-                s += sm_exp(v - m);
+                s += sm_exp<T>(v - m);
             }
         }
-        const C inv = C(1) / s, lse = sm_log(s);
+        const C inv = C(1) / s, lse = sm_log<T>(s);
         for (int64_t d = 0; d < D; ++d) {
             const C v = load_as<C>(xc[d * inner]);
-            yc[d * inner] = store_as<T>(log ? v - m - lse : sm_exp(v - m) * inv);
+            yc[d * inner] = store_as<T>(log ? v - m - lse : sm_exp<T>(v - m) * inv);
         }
     }
 }
@@ -418,7 +768,7 @@ __global__ void __launch_bounds__(THREADS) softmax_bwd_rows_reg(const T* __restr
             VT r;
 #pragma unroll
             for (int j = 0; j < V; ++j) {
-                r.v[j] = store_as<T>(log ? g[k][j] - sm_exp(o[k][j]) * acc : o[k][j] * (g[k][j] - acc));
+                r.v[j] = store_as<T>(log ? g[k][j] - sm_exp<T>(o[k][j]) * acc : o[k][j] * (g[k][j] - acc));
             }
             *reinterpret_cast<VT*>(dx + row * D + idx) = r;
         }
@@ -439,7 +789,7 @@ __global__ void __launch_bounds__(kThreads) softmax_bwd_rows_loop(const T* __res
     for (int64_t i = threadIdx.x; i < D; i += kThreads) {
         const C g = load_as<C>(dy[row * D + i]);
         const C o = load_as<C>(y[row * D + i]);
-        dx[row * D + i] = store_as<T>(log ? g - sm_exp(o) * acc : o * (g - acc));
+        dx[row * D + i] = store_as<T>(log ? g - sm_exp<T>(o) * acc : o * (g - acc));
     }
 }
 
@@ -461,7 +811,7 @@ __global__ void __launch_bounds__(kThreads) softmax_bwd_cols(const T* __restrict
         for (int64_t d = 0; d < D; ++d) {
             const C g = load_as<C>(dy[base + d * inner]);
             const C w = load_as<C>(y[base + d * inner]);
-            dx[base + d * inner] = store_as<T>(log ? g - sm_exp(w) * acc : w * (g - acc));
+            dx[base + d * inner] = store_as<T>(log ? g - sm_exp<T>(w) * acc : w * (g - acc));
         }
     }
 }
@@ -521,6 +871,178 @@ tpb_tensor dense_like(void* data, int dtype, int ndim, const int64_t* sizes) {
     return t;
 }
 
+// Column kernel: split R over blocks until the device is filled once with
+// resident blocks (at least 16 rows per split, at most 1024 splits).
+template <typename T, typename To, int OP>
+int col_splits(int64_t base_blocks, int64_t R, int dev, int sms) {
+    constexpr int V = VecWidth<T>::value;
+    static int blocks_per_sm[64] = {};
+    if (blocks_per_sm[dev] == 0) {
+        int n = 0;
+        TPB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, reduce_cols<T, To, OP, V>, kThreads, 0));
+        blocks_per_sm[dev] = std::max(n, 1);
+    }
+    const int64_t cap = int64_t(sms) * blocks_per_sm[dev];
+    if (base_blocks >= cap) return 1;
+    const int64_t splits = std::min<int64_t>((cap + base_blocks - 1) / base_blocks, std::max<int64_t>(R / 16, 1));
+    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(splits, 1024)));
+}
+
+template <typename T, typename To, int OP>
+void launch_cols(bool vec, const T* x, To* o, typename Acc<T>::type* partial, int64_t O, int64_t R, int64_t K,
+                 int64_t os, int64_t rs, int64_t kblocks, int splits, double count, cudaStream_t stream) {
+    using A = typename Acc<T>::type;
+    constexpr int V = VecWidth<T>::value;
+    dim3 grid(static_cast<unsigned>(kblocks), static_cast<unsigned>(O), static_cast<unsigned>(splits));
+    if (vec) {
+        reduce_cols<T, To, OP, V><<<grid, kThreads, 0, stream>>>(x, o, partial, O, R, K, os, rs, count);
+    } else {
+        reduce_cols<T, To, OP, 1><<<grid, kThreads, 0, stream>>>(x, o, partial, O, R, K, os, rs, count);
+    }
+    check_launch("reduce_cols");
+    if (splits > 1) {
+        const int64_t n = O * K;
+        const unsigned g2 = static_cast<unsigned>((n + 31) / 32);
+        reduce_col_partials<A, To, OP><<<g2, kThreads, 0, stream>>>(partial, o, n, splits, count);
+        check_launch("reduce_col_partials");
+    }
+}
+
+// Resident blocks of the block-per-row kernel on the whole device.
+template <typename T, typename To, int OP>
+int64_t rows_capacity(int dev, int sms) {
+    static int blocks_per_sm[64] = {};
+    if (blocks_per_sm[dev] == 0) {
+        int n = 0;
+        TPB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, reduce_rows<T, To, OP>, kThreads, 0));
+        blocks_per_sm[dev] = std::max(n, 1);
+    }
+    return int64_t(sms) * blocks_per_sm[dev];
+}
+
+// Whether the shared-memory ring is the default row kernel (measured
+// against the block kernel on the op sweep's shapes).
+constexpr bool ring_by_default() { return false; }
+
+// The completion ticket of `stream` on `dev`, or null (two-pass combine)
+// when none may be used: streams that are being captured into a graph (a
+// replay could run beside the stream's own launches), the per-thread default
+// stream (one handle, many streams) and more streams than slots.
+unsigned* reduce_ticket(int dev, cudaStream_t stream) {
+    if (stream == cudaStreamPerThread || dev < 0 || dev >= 64) return nullptr;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    TPB_CUDA(cudaStreamIsCapturing(stream, &cap));
+    if (cap != cudaStreamCaptureStatusNone) return nullptr;
+    static std::mutex lock;
+    static unsigned* base[64] = {};
+    static std::map<std::pair<int, cudaStream_t>, int> slots;
+    static int used[64] = {};
+    std::lock_guard<std::mutex> g(lock);
+    if (base[dev] == nullptr) {
+        void* p = nullptr;
+        TPB_CUDA(cudaGetSymbolAddress(&p, g_reduce_tickets));
+        base[dev] = static_cast<unsigned*>(p);
+    }
+    auto it = slots.find({dev, stream});
+    if (it == slots.end()) {
+        if (used[dev] >= kTicketSlots) return nullptr;
+        it = slots.emplace(std::make_pair(dev, stream), used[dev]++).first;
+    }
+    return base[dev] + it->second;
+}
+
+// Row-kernel plan.  Three kernels:
+//   ring  - rows on 16-byte boundaries with a uniform row stride, at least
+//           one 4 KB chunk long: streamed through shared memory by bulk
+//           copies (per-chunk partials when a row spans several chunks);
+//   warp  - many short rows (at most 4 KB): one warp per row;
+//   block - otherwise: a block per row; fewer rows than resident blocks are
+//           split into chunks (with a second pass over the partials).
+// TPB200_REDUCE_ROWS=ring|warp|block forces a kernel where its layout
+// conditions hold (for A/B measurements).
+enum RowKernel { kRowsBlock = 0, kRowsWarp = 1, kRowsRing = 2 };
+
+struct RowPlan {
+    RowKernel kind;
+    int splits;
+    int64_t chunk;
+    int64_t row_stride;
+};
+
+template <typename T>
+RowPlan plan_rows(const T* x, const DimGroup& kept_rows, int64_t rows, int64_t R, int sms, int64_t cap) {
+    constexpr int V = VecWidth<T>::value;
+    static const char* force = std::getenv("TPB200_REDUCE_ROWS");
+    const bool f_ring = force != nullptr && std::strcmp(force, "ring") == 0;
+    const bool f_warp = force != nullptr && std::strcmp(force, "warp") == 0;
+    const bool f_block = force != nullptr && std::strcmp(force, "block") == 0;
+    RowPlan p{kRowsBlock, 1, R, 0};
+    const int64_t row_bytes = R * int64_t(sizeof(T));
+    const int64_t stride = rows == 1 || kept_rows.n == 0 ? 0 : kept_rows.n == 1 ? kept_rows.strides[0] : -1;
+    const bool ring_ok = aligned16(x) && stride >= 0 && (stride * int64_t(sizeof(T))) % 16 == 0 &&
+                         row_bytes >= 4096;
+    if (ring_ok && (f_ring || (!f_warp && !f_block && ring_by_default()))) {
+        p.kind = kRowsRing;
+        p.chunk = kChunkBytes / sizeof(T);
+        p.splits = static_cast<int>((R + p.chunk - 1) / p.chunk);
+        p.row_stride = stride;
+        return p;
+    }
+    if (f_warp || (!f_block && row_bytes <= 4096 && rows >= int64_t(sms) * 32)) {
+        p.kind = kRowsWarp;
+        return p;
+    }
+    // Fewer rows than resident blocks (`cap`): split each row over enough
+    // blocks to fill the device once (the interleaved sweep keeps the splits
+    // equal), each split keeping at least four vectors per thread.
+    if (rows < cap) {
+        p.splits = static_cast<int>(std::min<int64_t>((cap + rows - 1) / rows,
+                                                      std::max<int64_t>(R / (kThreads * V * 4), 1)));
+    }
+    return p;
+}
+
+template <typename T, typename To, int OP>
+void launch_rows(const RowPlan& p, const T* x, To* o, typename Acc<T>::type* partial,
+                 const OffsetCalc<1>& calc, int64_t rows, int64_t R, double count, int dev, int sms,
+                 cudaStream_t stream) {
+    using A = typename Acc<T>::type;
+    if (p.kind == kRowsWarp) {
+        const unsigned grid = static_cast<unsigned>(
+            std::min<int64_t>((rows + kWarpsPerBlock - 1) / kWarpsPerBlock, int64_t(sms) * 8));
+        reduce_rows_warp<T, To, OP><<<grid, kThreads, 0, stream>>>(x, o, calc, rows, R, count);
+        check_launch("reduce_rows_warp");
+        return;
+    }
+    if (p.kind == kRowsRing) {
+        auto kern = reduce_rows_ring<T, To, OP>;
+        constexpr size_t smem = size_t(kReduceStages) * kChunkBytes;
+        static int blocks_per_sm[64] = {};
+        if (blocks_per_sm[dev] == 0) {
+            TPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+            int n = 0;
+            TPB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, smem));
+            blocks_per_sm[dev] = std::max(n, 1);
+        }
+        const int64_t items = rows * p.splits;
+        const unsigned grid = static_cast<unsigned>(std::min<int64_t>(items, int64_t(sms) * blocks_per_sm[dev]));
+        kern<<<grid, kThreads, smem, stream>>>(x, o, partial, rows, R, p.row_stride, p.chunk, p.splits, count,
+                                               device_error_word(dev));
+        check_launch("reduce_rows_ring");
+    } else {
+        unsigned* ticket = rows == 1 && p.splits > 1 ? reduce_ticket(dev, stream) : nullptr;
+        reduce_rows<T, To, OP><<<static_cast<unsigned>(rows * p.splits), kThreads, 0, stream>>>(
+            x, o, partial, calc, R, p.splits, count, ticket);
+        check_launch("reduce_rows");
+        if (ticket != nullptr) return;
+    }
+    if (p.splits > 1) {
+        reduce_row_partials<A, To, OP><<<static_cast<unsigned>(rows), kThreads, 0, stream>>>(
+            partial, o, p.splits, count);
+        check_launch("reduce_row_partials");
+    }
+}
+
 template <typename T, typename To, int OP>
 void reduce_launch(const tpb_tensor& out, const tpb_tensor& xin, uint32_t mask, int dev,
                    cudaStream_t stream) {
@@ -558,34 +1080,10 @@ void reduce_launch(const tpb_tensor& out, const tpb_tensor& xin, uint32_t mask, 
         const int vw = vec ? V : 1;
         const int64_t kblocks = (K / vw + kThreads - 1) / kThreads;
         if (O < 65536) {
-            int splits = 1;
-            const int64_t base_blocks = kblocks * O;
-            const int64_t want = int64_t(sms) * 4;
-            if (base_blocks < want) {
-                splits = static_cast<int>(std::min<int64_t>((want + base_blocks - 1) / base_blocks,
-                                                            std::max<int64_t>(R / 16, 1)));
-                splits = std::min(splits, 1024);
-            }
-            const int64_t rchunk = (R + splits - 1) / splits;
-            splits = static_cast<int>((R + rchunk - 1) / rchunk);
-            if (splits < 1) splits = 1;
+            const int splits = col_splits<T, To, OP>(kblocks * O, R, dev, sms);
             Scratch partial(splits > 1 ? sizeof(A) * splits * O * K : 0, dev, stream);
-            dim3 grid(static_cast<unsigned>(kblocks), static_cast<unsigned>(O), static_cast<unsigned>(splits));
-            if (vec) {
-                reduce_cols<T, To, OP, V><<<grid, kThreads, 0, stream>>>(
-                    x, o, static_cast<A*>(partial.get()), O, R, K, os, rs, rchunk, count);
-            } else {
-                reduce_cols<T, To, OP, 1><<<grid, kThreads, 0, stream>>>(
-                    x, o, static_cast<A*>(partial.get()), O, R, K, os, rs, rchunk, count);
-            }
-            check_launch("reduce_cols");
-            if (splits > 1) {
-                const int64_t n = O * K;
-                const unsigned g2 = static_cast<unsigned>(std::min<int64_t>(blocks_for(n, kThreads), sms * 8));
-                reduce_col_partials<A, To, OP><<<g2, kThreads, 0, stream>>>(
-                    static_cast<const A*>(partial.get()), o, n, splits, count);
-                check_launch("reduce_col_partials");
-            }
+            launch_cols<T, To, OP>(vec, x, o, static_cast<A*>(partial.get()), O, R, K, os, rs, kblocks, splits,
+                                   count, stream);
             return;
         }
     }
@@ -623,25 +1121,9 @@ void reduce_launch(const tpb_tensor& out, const tpb_tensor& xin, uint32_t mask, 
               (long long)rows);
     const int which[1] = {0};
     const auto calc = OffsetCalc<1>::make(group_layout(kept_rows), which);
-    int splits = 1;
-    const int64_t want = int64_t(sms) * 4;
-    if (rows < want) {
-        splits = static_cast<int>(std::min<int64_t>((want + rows - 1) / rows,
-                                                    std::max<int64_t>(R / (kThreads * V * 4), 1)));
-    }
-    int64_t chunk = (R + splits - 1) / splits;
-    chunk = (chunk + V - 1) / V * V;
-    if (chunk < 1) chunk = 1;
-    splits = static_cast<int>(std::max<int64_t>((R + chunk - 1) / chunk, 1));
-    Scratch partial(splits > 1 ? sizeof(A) * rows * splits : 0, dev, stream);
-    reduce_rows<T, To, OP><<<static_cast<unsigned>(rows * splits), kThreads, 0, stream>>>(
-        x, o, static_cast<A*>(partial.get()), calc, R, splits, chunk, count);
-    check_launch("reduce_rows");
-    if (splits > 1) {
-        reduce_row_partials<A, To, OP><<<static_cast<unsigned>(rows), kThreads, 0, stream>>>(
-            static_cast<const A*>(partial.get()), o, splits, count);
-        check_launch("reduce_row_partials");
-    }
+    const RowPlan plan = plan_rows<T>(x, kept_rows, rows, R, sms, rows_capacity<T, To, OP>(dev, sms));
+    Scratch partial(plan.splits > 1 ? sizeof(A) * rows * plan.splits : 0, dev, stream);
+    launch_rows<T, To, OP>(plan, x, o, static_cast<A*>(partial.get()), calc, rows, R, count, dev, sms, stream);
 }
 
 template <typename A> struct AccCode;
@@ -679,6 +1161,71 @@ void reduce_op_dispatch(int op, const tpb_tensor& out, const tpb_tensor& x, uint
     }
 }
 
+// Which row kernel: the shared-memory ring for many rows of 16-bit
+// elements (whose per-row work is short next to the HBM latency), the
+// one-block-per-row kernel otherwise.  TPB200_SOFTMAX=ring|reg overrides the
+// choice (for A/B measurements).
+bool use_softmax_ring(size_t elem_size, int64_t rows, int dev) {
+    static const char* force = std::getenv("TPB200_SOFTMAX");
+    if (rows < int64_t(num_sms(dev)) * 2) return false;
+    if (force != nullptr && std::strcmp(force, "ring") == 0) return true;
+    if (force != nullptr && std::strcmp(force, "reg") == 0) return false;
+    return elem_size == 2;
+}
+
+// About 48 KB of rows per block in the ring (at least two stages): with the
+// blocks an SM holds that keeps 100+ KB of reads in flight per SM.
+constexpr uint32_t kRingBytes = 48 * 1024;
+constexpr int kRingMaxSmem = 64 * 1024;  // two stages of a 32 KB row
+
+template <typename T, int V, int VPT, int THREADS, bool LOG>
+void launch_ring(T* y, const T* x, int64_t rows, int64_t D, int dev, cudaStream_t stream) {
+    auto kern = softmax_rows_ring<T, V, VPT, THREADS, LOG>;
+    const uint32_t stage_bytes = (static_cast<uint32_t>(D * sizeof(T)) + 127u) & ~127u;
+    const int stages = std::max(2, std::min<int>(kMaxRingStages, static_cast<int>(kRingBytes / stage_bytes)));
+    const size_t smem = size_t(stages) * stage_bytes;
+    TPB_CHECK(smem <= size_t(kRingMaxSmem), "softmax: ring of %zu bytes", smem);
+    static int blocks_per_sm[64][kMaxRingStages + 1] = {};
+    int& nb = blocks_per_sm[dev][stages];
+    if (nb == 0) {
+        TPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kRingMaxSmem));
+        int n = 0;
+        TPB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, THREADS, smem));
+        nb = std::max(n, 1);
+    }
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(rows, int64_t(num_sms(dev)) * nb));
+    kern<<<grid, THREADS, smem, stream>>>(x, y, rows, D, stages, device_error_word(dev));
+    check_launch("softmax_rows_ring");
+}
+
+// Row kernels by row length: VPT vectors per thread of a 256- or 512-thread
+// block; rows longer than 2048 vectors take the online two-pass kernel.
+template <typename T, bool LOG>
+void softmax_rows_launch(T* y, const T* x, int64_t rows, int64_t D, int dev, cudaStream_t stream) {
+    constexpr int V = VecWidth<T>::value;
+    const unsigned grid = static_cast<unsigned>(rows);
+    const bool vec = D % V == 0 && aligned16(x) && aligned16(y);
+    const int64_t nv = D / V;
+    if (vec && nv <= 2048 && use_softmax_ring(sizeof(T), rows, dev)) {
+        if (nv <= 256) launch_ring<T, V, 1, 256, LOG>(y, x, rows, D, dev, stream);
+        else if (nv <= 512) launch_ring<T, V, 2, 256, LOG>(y, x, rows, D, dev, stream);
+        else if (nv <= 1024) launch_ring<T, V, 4, 256, LOG>(y, x, rows, D, dev, stream);
+        else launch_ring<T, V, 4, 512, LOG>(y, x, rows, D, dev, stream);
+        return;
+    }
+    if (vec && nv <= 2048) {
+        if (nv <= 256) softmax_rows_reg<T, V, 1, 256, LOG><<<grid, 256, 0, stream>>>(x, y, D);
+        else if (nv <= 512) softmax_rows_reg<T, V, 2, 256, LOG><<<grid, 256, 0, stream>>>(x, y, D);
+        else if (nv <= 1024) softmax_rows_reg<T, V, 4, 256, LOG><<<grid, 256, 0, stream>>>(x, y, D);
+        else softmax_rows_reg<T, V, 4, 512, LOG><<<grid, 512, 0, stream>>>(x, y, D);
+    } else if (!vec && D <= 1024) {
+        softmax_rows_reg<T, 1, 4, 256, LOG><<<grid, 256, 0, stream>>>(x, y, D);
+    } else {
+        softmax_rows_online<T><<<grid, kThreads, 0, stream>>>(x, y, D, LOG);
+    }
+    check_launch("softmax_rows");
+}
+
 template <typename T>
 void softmax_launch(bool log, T* y, const T* x, int64_t outer, int64_t D, int64_t inner, int dev,
                     cudaStream_t stream) {
@@ -689,23 +1236,9 @@ void softmax_launch(bool log, T* y, const T* x, int64_t outer, int64_t D, int64_
         check_launch("softmax_cols");
         return;
     }
-    constexpr int V = VecWidth<T>::value;
-    const unsigned rows = static_cast<unsigned>(outer);
     TPB_CHECK(outer < (int64_t(1) << 31), "softmax: too many rows");
-    const bool vec = D % V == 0 && aligned16(x) && aligned16(y);
-    if (vec) {
-        const int64_t nv = D / V;
-        if (nv <= 256) softmax_rows_reg<T, V, 1, 256><<<rows, 256, 0, stream>>>(x, y, D, log);
-        else if (nv <= 512) softmax_rows_reg<T, V, 2, 256><<<rows, 256, 0, stream>>>(x, y, D, log);
-        else if (nv <= 1024) softmax_rows_reg<T, V, 4, 256><<<rows, 256, 0, stream>>>(x, y, D, log);
-        else if (nv <= 2048) softmax_rows_reg<T, V, 4, 512><<<rows, 512, 0, stream>>>(x, y, D, log);
-        else softmax_rows_online<T><<<rows, kThreads, 0, stream>>>(x, y, D, log);
-    } else if (D <= 1024) {
-        softmax_rows_reg<T, 1, 4, 256><<<rows, 256, 0, stream>>>(x, y, D, log);
-    } else {
-        softmax_rows_online<T><<<rows, kThreads, 0, stream>>>(x, y, D, log);
-    }
-    check_launch("softmax_rows");
+    if (log) softmax_rows_launch<T, true>(y, x, outer, D, dev, stream);
+    else softmax_rows_launch<T, false>(y, x, outer, D, dev, stream);
 }
 
 template <typename T>
@@ -854,33 +1387,9 @@ void reduce_launch_noalloc(const tpb_tensor& out, const tpb_tensor& xin, uint32_
         const int64_t kblocks = (K / vw + kThreads - 1) / kThreads;
         TPB_CHECK(O < 65536, "reduce_noalloc: %lld outer rows exceed the column kernel's grid",
                   (long long)O);
-        int splits = 1;
-        const int64_t base_blocks = kblocks * O;
-        const int64_t want = int64_t(sms) * 4;
-        if (base_blocks < want) {
-            splits = static_cast<int>(std::min<int64_t>((want + base_blocks - 1) / base_blocks,
-                                                        std::max<int64_t>(R / 16, 1)));
-            splits = std::min(splits, 1024);
-        }
-        const int64_t rchunk = (R + splits - 1) / splits;
-        splits = static_cast<int>((R + rchunk - 1) / rchunk);
-        if (splits < 1) splits = 1;
+        const int splits = col_splits<T, To, OP>(kblocks * O, R, dev, sms);
         if (splits > 1) check_noalloc_fit(sizeof(A) * splits * O * K);
-        dim3 grid(static_cast<unsigned>(kblocks), static_cast<unsigned>(O), static_cast<unsigned>(splits));
-        if (vec) {
-            reduce_cols<T, To, OP, V><<<grid, kThreads, 0, stream>>>(x, o, partial, O, R, K, os, rs,
-                                                                      rchunk, count);
-        } else {
-            reduce_cols<T, To, OP, 1><<<grid, kThreads, 0, stream>>>(x, o, partial, O, R, K, os, rs,
-                                                                      rchunk, count);
-        }
-        check_launch("reduce_cols");
-        if (splits > 1) {
-            const int64_t n = O * K;
-            const unsigned g2 = static_cast<unsigned>(std::min<int64_t>(blocks_for(n, kThreads), sms * 8));
-            reduce_col_partials<A, To, OP><<<g2, kThreads, 0, stream>>>(partial, o, n, splits, count);
-            check_launch("reduce_col_partials");
-        }
+        launch_cols<T, To, OP>(vec, x, o, partial, O, R, K, os, rs, kblocks, splits, count, stream);
         return;
     }
     const bool rows_ok = red.n == 0 || (red.n == 1 && red.strides[0] == 1);
@@ -892,25 +1401,9 @@ void reduce_launch_noalloc(const tpb_tensor& out, const tpb_tensor& xin, uint32_
     TPB_CHECK(rows < (int64_t(1) << 31), "reduce_noalloc: too many output elements");
     const int which[1] = {0};
     const auto calc = OffsetCalc<1>::make(group_layout(kept), which);
-    int splits = 1;
-    const int64_t want = int64_t(sms) * 4;
-    if (rows < want) {
-        splits = static_cast<int>(std::min<int64_t>((want + rows - 1) / rows,
-                                                    std::max<int64_t>(R / (kThreads * V * 4), 1)));
-    }
-    int64_t chunk = (R + splits - 1) / splits;
-    chunk = (chunk + V - 1) / V * V;
-    if (chunk < 1) chunk = 1;
-    splits = static_cast<int>(std::max<int64_t>((R + chunk - 1) / chunk, 1));
-    if (splits > 1) check_noalloc_fit(sizeof(A) * rows * splits);
-    reduce_rows<T, To, OP><<<static_cast<unsigned>(rows * splits), kThreads, 0, stream>>>(
-        x, o, partial, calc, R, splits, chunk, count);
-    check_launch("reduce_rows");
-    if (splits > 1) {
-        reduce_row_partials<A, To, OP><<<static_cast<unsigned>(rows), kThreads, 0, stream>>>(
-            partial, o, splits, count);
-        check_launch("reduce_row_partials");
-    }
+    const RowPlan plan = plan_rows<T>(x, kept, rows, R, sms, rows_capacity<T, To, OP>(dev, sms));
+    if (plan.splits > 1) check_noalloc_fit(sizeof(A) * rows * plan.splits);
+    launch_rows<T, To, OP>(plan, x, o, partial, calc, rows, R, count, dev, sms, stream);
 }
 
 template <typename T, int OP>

@@ -175,6 +175,53 @@ def test_float32_matmul_precision_selects_tf32(ops):
     assert fast > exact  # the switch really selected another path
 
 
+class _Highest:
+    """fp32 products at full precision (no TF32) inside the block."""
+
+    def __enter__(self):
+        self.previous = torch.get_float32_matmul_precision()
+        torch.set_float32_matmul_precision("highest")
+
+    def __exit__(self, *exc):
+        torch.set_float32_matmul_precision(self.previous)
+
+
+def test_fp32_split_tf32_layouts_and_epilogue(ops):
+    # Large enough for the split-TF32 tensor-core path: transposed operands
+    # (copied K-major first), an operand broadcast over the batch, and the
+    # addmm epilogue (alpha, beta, bias).
+    with _Highest():
+        a, b = rand(640, 384, seed=1), rand(384, 520, seed=2)
+        got = ops.mm(dev(ops, a.t().contiguous()).t(), dev(ops, b.t().contiguous()).t())
+        assert check_sampled(got, a, b) <= 1e-5
+        a2, b2 = rand(512, 256, seed=3), rand(4, 256, 512, seed=4)
+        got = ops.matmul(dev(ops, a2), dev(ops, b2))
+        assert check_sampled(got, a2.expand(4, 512, 256), b2) <= 1e-5
+        bias = rand(520, seed=5)
+        got = ops.addmm(dev(ops, bias), dev(ops, a), dev(ops, b), beta=0.5, alpha=2.0)
+        assert check_sampled(got, a, b, bias, 2.0, 0.5) <= 1e-5
+
+
+def test_fp32_split_tf32_non_finite_inputs(ops):
+    # inf and NaN keep fp32 semantics (inf * finite = inf, not the NaN a
+    # zero low part would give); every other output stays exact.
+    a, b = rand(512, 512, seed=1), rand(512, 512, seed=2)
+    a[3, 7] = float("inf")
+    a[100, 5] = float("nan")
+    b[9, 200] = -float("inf")
+    b[:, 300] = 1.0  # exactly representable: zero low parts in that column
+    a[50, 11] = float("inf")
+    with _Highest():
+        got = ops.mm(dev(ops, a), dev(ops, b)).cpu()
+    want = O.gemm(a.double(), b.double()).float()
+    assert torch.equal(torch.isnan(got), torch.isnan(want))
+    assert torch.equal(torch.isinf(got), torch.isinf(want))
+    inf = torch.isinf(want)
+    assert torch.equal(got[inf], want[inf])
+    fin = torch.isfinite(want)
+    assert (got[fin] - want[fin]).abs().max().item() <= 1e-5 * max(want[fin].abs().max().item(), 1.0)
+
+
 # ------------------------------------------------- BASELINE GEMM shapes --
 
 def test_baseline_mm_8192_bf16(ops):

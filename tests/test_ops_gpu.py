@@ -234,6 +234,25 @@ def test_row_broadcast_fast_path_shapes(ops):
         assert_close(ops.mul_Tensor(dev(ops, b), dev(ops, a)), O.binary(O.MUL, b.expand(33, n), a))
 
 
+@pytest.mark.parametrize("dtype", FLOATS + [torch.float64, torch.int32])
+def test_row_broadcast_long_rows_both_orders(ops, dtype):
+    # Rows of at least half a block of vectors take the 2-d kernel (one row
+    # read per several outputs); outer counts not a multiple of its row group,
+    # and the row as first and as second operand of non-commuting ops.
+    for outer, n in ((37, 1024), (5, 4096), (2, 8192), (9, 2048)):
+        if dtype.is_floating_point:
+            a, b = rand(outer, n, dtype=dtype, seed=6), (rand(n, dtype=dtype, seed=7).abs() + 0.5).to(dtype)
+        else:
+            a, b = randint(outer, n, dtype=dtype, seed=6), randint(n, low=1, high=50, dtype=dtype, seed=7)
+        da, db = dev(ops, a), dev(ops, b)
+        assert_close(ops.sub_Tensor(da, db), O.binary(O.SUB, a, b.expand(outer, n)), dtype)
+        assert_close(ops.sub_Tensor(db, da), O.binary(O.SUB, b.expand(outer, n), a), dtype)
+        if dtype.is_floating_point:
+            apos = (a.abs() + 0.5).to(dtype)  # divisor away from zero
+            assert_close(ops.div_Tensor(da, db), O.binary(O.DIV, a, b.expand(outer, n)), dtype)
+            assert_close(ops.div_Tensor(db, dev(ops, apos)), O.binary(O.DIV, b.expand(outer, n), apos), dtype)
+
+
 # ----------------------------------------------------------------- unary --
 
 UN = {"exp": O.EXP, "log": O.LOG, "sqrt": O.SQRT, "rsqrt": O.RSQRT, "neg": O.NEG, "abs": O.ABS,
@@ -395,6 +414,60 @@ def test_softmax_row_lengths(ops, D):
         x = a.to(dtype)
         assert_close(ops.softmax(dev(ops, x), -1), O.softmax(x, -1), dtype)
         assert_close(ops._log_softmax(dev(ops, x), -1), O.softmax(x, -1, True), dtype)
+
+
+@pytest.mark.parametrize("dtype", FLOATS + [torch.float64])
+@pytest.mark.parametrize("rows,D", [(297, 8), (640, 1000), (333, 2048), (1200, 4096), (301, 8192)])
+def test_softmax_many_rows(ops, dtype, rows, D):
+    # Enough rows for the persistent kernel that stages rows in shared memory.
+    a = rand(rows, D, dtype=dtype, scale=3.0)
+    d = dev(ops, a)
+    assert_close(ops.softmax(d, -1), O.softmax(a, -1), dtype)
+    assert_close(ops._log_softmax(d, -1), O.softmax(a, -1, True), dtype)
+
+
+def test_full_reductions_on_concurrent_streams(ops):
+    # Full reductions split over the grid finish in their last block, which
+    # counts the blocks in on a per-stream ticket: launches queued on two
+    # streams at once, several times in a row, each keep their own count.
+    a = rand(4096, 4096, seed=11)
+    b = rand(4096, 4096, seed=12, scale=3.0)
+    da, db = dev(ops, a), dev(ops, b)
+    want_a, want_b = O.reduce(O.SUM, a, None, torch.float32), O.reduce(O.AMAX, b, None, torch.float32)
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    torch.cuda.synchronize()
+    outs = []
+    for _ in range(4):
+        with torch.cuda.stream(s1):
+            ra = ops.sum(da)
+        with torch.cuda.stream(s2):
+            rb = ops.amax(db)
+        outs.append((ra, rb))
+    torch.cuda.synchronize()
+    for ra, rb in outs:
+        assert_close(ra, want_a, torch.float32, scale=20)
+        assert_equal(host(ops, rb), want_b)
+
+
+@pytest.mark.parametrize("dtype", FLOATS + [torch.float64, torch.int32])
+def test_many_row_reductions(ops, dtype):
+    # Enough rows for one warp per row, including rows that start off a
+    # 16-byte boundary (a column slice) and rows shorter than a warp.
+    for shape, sl in (((5000, 37), None), ((6000, 1000), None), ((4800, 131), 1), ((8192, 4096), None)):
+        if dtype.is_floating_point:
+            full = rand(*shape, dtype=dtype)
+        else:
+            full = randint(*shape, low=-1000, high=1000, dtype=dtype)
+        a = full[:, sl:] if sl else full
+        d = dev(ops, full)
+        d = d[:, sl:] if sl else d
+        if dtype.is_floating_point:
+            assert_close(ops.sum_dim_IntList(d, [1]), O.reduce(O.SUM, a, [1], dtype), dtype, scale=20)
+            assert_close(ops.mean_dim(d, [-1]), O.reduce(O.MEAN, a, [1], dtype), dtype)
+        else:
+            assert_equal(host(ops, ops.sum_dim_IntList(d, [1])), O.reduce(O.SUM, a, [1], torch.int64))
+        assert_equal(host(ops, ops.amax(d, [-1])), O.reduce(O.AMAX, a, [1], dtype))
+        assert_equal(host(ops, ops.amin(d, [1])), O.reduce(O.AMIN, a, [1], dtype))
 
 
 def test_memory_statistics(backend, ops):

@@ -48,7 +48,7 @@ def _pair(op, x, dims, out_dtype):
 
 CASES = [
     # (shape, dtype, dims, op, out dtype) -- each uses per-block partial results
-    ((8192, 8192), torch.float32, [0, 1], SUM, torch.float32),        # full reduction, 592 splits
+    ((8192, 8192), torch.float32, [0, 1], SUM, torch.float32),        # full reduction, thousands of splits
     ((8192, 16384), torch.bfloat16, [0], SUM, torch.bfloat16),        # bias-gradient column sum
     ((16, 65536), torch.float32, [1], MEAN, torch.float32),           # few long rows
     ((2, 4096, 2), torch.float16, [1], SUM, torch.float16),           # [O, R, K] columns
