@@ -405,6 +405,9 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     gemm_ms = [s.elapsed_time(e) for s, e in model.gemm_events]
     model.gemm_events = None
     gemm_avg_ms = sum(gemm_ms) / len(gemm_ms)
+    # Average per GEMM of the step, in step order: h = x W1^T, out = a W2^T,
+    # dW2 = dout^T a, d_a = dout W2, dW1 = dh^T x.
+    per_gemm = [sum(gemm_ms[i::5]) / len(gemm_ms[i::5]) for i in range(5)]
     loss_value = ops.item(loss)
 
     # ---- end to end: pinned host batches, copies and the loss read-back timed
@@ -474,7 +477,9 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                          "frac": round(achieved / bf16_sustained, 3), "traffic": traffic,
                          "peak_kind": f"{peak_kind} sustained bf16 (kernel timed inside a long step)",
                          "per_launch_flops": gemm_flops, "avg_launch_ms": round(gemm_avg_ms, 4),
-                         "launches_timed": len(gemm_ms)},
+                         "launches_timed": len(gemm_ms),
+                         "per_gemm_ms": {k: round(v, 4) for k, v in zip(
+                             ("h=xW1^T", "out=aW2^T", "dW2=dout^T a", "da=dout W2", "dW1=dh^T x"), per_gemm)}},
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 4),
                     "path": "pinned host batch -> tp_b200_memcpy (copy stream, next batch prefetched) "

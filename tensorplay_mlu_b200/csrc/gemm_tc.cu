@@ -189,6 +189,42 @@ template <int BN> struct TcShape {
     static constexpr int kTmemCols = 2 * BN;  // two accumulators (power of two)
 };
 
+// One operand's share of a pipeline stage: `rows` rows (M or N) by kEPR
+// K-elements, written in the 128-byte-swizzled layout the MMA descriptors
+// describe.  K-major: 64-row boxes (dst row r at r * 128 B).  MN-major: boxes
+// of kEPR (MN) x kEPR (K), one per kEPR-wide MN chunk (chunk j at j * kChunk).
+// The layout and batching are compile-time so the producer's loop is
+// straight-line code.
+constexpr int kBoxRows = 64;
+
+template <int ES, bool MN, bool BATCHED, bool PAIR>
+__device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap* map, uint32_t bar, int mn0, int k0,
+                                             int b, int rows) {
+    constexpr int kEPR = 128 / ES;
+    constexpr uint32_t kChunk = kEPR * 128;
+    if constexpr (MN) {
+        for (int j = 0; j < rows / kEPR; ++j) {
+            if constexpr (PAIR) {
+                if constexpr (BATCHED) tma_load_3d_pair(dst + j * kChunk, map, bar, mn0 + j * kEPR, k0, b);
+                else tma_load_2d_pair(dst + j * kChunk, map, bar, mn0 + j * kEPR, k0);
+            } else {
+                if constexpr (BATCHED) tma_load_3d(dst + j * kChunk, map, bar, mn0 + j * kEPR, k0, b);
+                else tma_load_2d(dst + j * kChunk, map, bar, mn0 + j * kEPR, k0);
+            }
+        }
+    } else {
+        for (int j = 0; j < rows / kBoxRows; ++j) {
+            if constexpr (PAIR) {
+                if constexpr (BATCHED) tma_load_3d_pair(dst + j * kBoxRows * 128, map, bar, k0, mn0 + j * kBoxRows, b);
+                else tma_load_2d_pair(dst + j * kBoxRows * 128, map, bar, k0, mn0 + j * kBoxRows);
+            } else {
+                if constexpr (BATCHED) tma_load_3d(dst + j * kBoxRows * 128, map, bar, k0, mn0 + j * kBoxRows, b);
+                else tma_load_2d(dst + j * kBoxRows * 128, map, bar, k0, mn0 + j * kBoxRows);
+            }
+        }
+    }
+}
+
 template <typename T, int BN>
 constexpr size_t tc_smem_bytes() {
     return size_t(TcShape<BN>::kStages) * (kBM * 128 + BN * 128) + 1024 + 256;
@@ -207,7 +243,7 @@ __device__ __forceinline__ void tile_coords(const TcParams& p, int tile, int& b,
     nt = q / gsize;
 }
 
-template <typename T, int BN>
+template <typename T, int BN, bool A_MN, bool B_MN, bool BATCHED>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const TcParams p) {
@@ -281,24 +317,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t da = smem_addr(smem_a + stage * kABytes);
                     const uint32_t db = smem_addr(smem_b + stage * kBBytes);
                     const int k0 = kb * kEPR;
-                    if (p.a_mn) {
-                        for (int j = 0; j < kBM / kEPR; ++j) {
-                            if (p.batched) tma_load_3d(da + j * kChunk, &tmA, fb, m0 + j * kEPR, k0, b);
-                            else tma_load_2d(da + j * kChunk, &tmA, fb, m0 + j * kEPR, k0);
-                        }
-                    } else {
-                        if (p.batched) tma_load_3d(da, &tmA, fb, k0, m0, b);
-                        else tma_load_2d(da, &tmA, fb, k0, m0);
-                    }
-                    if (p.b_mn) {
-                        for (int j = 0; j < BN / kEPR; ++j) {
-                            if (p.batched) tma_load_3d(db + j * kChunk, &tmB, fb, n0 + j * kEPR, k0, b);
-                            else tma_load_2d(db + j * kChunk, &tmB, fb, n0 + j * kEPR, k0);
-                        }
-                    } else {
-                        if (p.batched) tma_load_3d(db, &tmB, fb, k0, n0, b);
-                        else tma_load_2d(db, &tmB, fb, k0, n0);
-                    }
+                    load_operand<E::kES, A_MN, BATCHED, false>(da, &tmA, fb, m0, k0, b, kBM);
+                    load_operand<E::kES, B_MN, BATCHED, false>(db, &tmB, fb, n0, k0, b, BN);
                     if (++stage == kStages) {
                         stage = 0;
                         phase ^= 1;
@@ -324,10 +344,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             int local = 0;
             bool ok = true;
-            const uint32_t a_lbo = p.a_mn ? kChunk : 16;
-            const uint32_t b_lbo = p.b_mn ? kChunk : 16;
-            const uint32_t a_kstep = p.a_mn ? kUmmaK * 128 : 32;
-            const uint32_t b_kstep = p.b_mn ? kUmmaK * 128 : 32;
+            constexpr uint32_t a_lbo = A_MN ? kChunk : 16;
+            constexpr uint32_t b_lbo = B_MN ? kChunk : 16;
+            constexpr uint32_t a_kstep = A_MN ? kUmmaK * 128 : 32;
+            constexpr uint32_t b_kstep = B_MN ? kUmmaK * 128 : 32;
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++local) {
                 const int acc = local & 1;
                 const uint32_t acc_phase = (local >> 1) & 1;
@@ -478,24 +498,6 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
-__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                                 int c0, int c1) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
-        : "memory");
-}
-
-__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                                 int c0, int c1, int c2) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
-        : "memory");
-}
-
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
                  "r"(ncols)
@@ -560,7 +562,7 @@ __device__ __forceinline__ void tile_coords_pair(const TcParams& p, int tile, in
     nt = q / gsize;
 }
 
-template <typename T>
+template <typename T, bool A_MN, bool B_MN, bool BATCHED>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const TcParams p, const int group_m) {
@@ -640,24 +642,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     const uint32_t da = smem_addr(smem_a + stage * kABytes);
                     const uint32_t db = smem_addr(smem_b + stage * kBBytes);
                     const int k0 = kb * kEPR;
-                    if (p.a_mn) {
-                        for (int j = 0; j < 128 / kEPR; ++j) {
-                            if (p.batched) tma_load_3d_pair(da + j * kChunk, &tmA, fb, m0 + j * kEPR, k0, b);
-                            else tma_load_2d_pair(da + j * kChunk, &tmA, fb, m0 + j * kEPR, k0);
-                        }
-                    } else {
-                        if (p.batched) tma_load_3d_pair(da, &tmA, fb, k0, m0, b);
-                        else tma_load_2d_pair(da, &tmA, fb, k0, m0);
-                    }
-                    if (p.b_mn) {
-                        for (int j = 0; j < 128 / kEPR; ++j) {
-                            if (p.batched) tma_load_3d_pair(db + j * kChunk, &tmB, fb, n0 + j * kEPR, k0, b);
-                            else tma_load_2d_pair(db + j * kChunk, &tmB, fb, n0 + j * kEPR, k0);
-                        }
-                    } else {
-                        if (p.batched) tma_load_3d_pair(db, &tmB, fb, k0, n0, b);
-                        else tma_load_2d_pair(db, &tmB, fb, k0, n0);
-                    }
+                    load_operand<E::kES, A_MN, BATCHED, true>(da, &tmA, fb, m0, k0, b, 128);
+                    load_operand<E::kES, B_MN, BATCHED, true>(db, &tmB, fb, n0, k0, b, 128);
                     if (++stage == kStages) {
                         stage = 0;
                         phase ^= 1;
@@ -673,10 +659,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             int local = 0;
             bool ok = true;
-            const uint32_t a_lbo = p.a_mn ? kChunk : 16;
-            const uint32_t b_lbo = p.b_mn ? kChunk : 16;
-            const uint32_t a_kstep = p.a_mn ? kUmmaK * 128 : 32;
-            const uint32_t b_kstep = p.b_mn ? kUmmaK * 128 : 32;
+            constexpr uint32_t a_lbo = A_MN ? kChunk : 16;
+            constexpr uint32_t b_lbo = B_MN ? kChunk : 16;
+            constexpr uint32_t a_kstep = A_MN ? kUmmaK * 128 : 32;
+            constexpr uint32_t b_kstep = B_MN ? kUmmaK * 128 : 32;
             for (int tile = cluster_id; tile < p.num_tiles && ok; tile += num_clusters, ++local) {
                 const int acc = local & 1;
                 const uint32_t acc_phase = (local >> 1) & 1;
@@ -861,14 +847,14 @@ int choose_bn(int64_t M, int64_t N, int64_t batch, int sms) {
     return bn;
 }
 
-template <typename T, int BN>
+template <typename T, int BN, bool A_MN, bool B_MN, bool BATCHED>
 void launch_tc(const GemmProblem& p, const CUtensorMap& ma, const CUtensorMap& mb, TcParams& tp,
                int dev, cudaStream_t stream) {
     constexpr size_t smem = tc_smem_bytes<T, BN>();
+    auto kern = gemm_tc_kernel<T, BN, A_MN, B_MN, BATCHED>;
     static bool configured[64] = {};
     if (!configured[dev]) {
-        TPB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(smem)));
+        TPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
         configured[dev] = true;
     }
     tp.m_tiles = static_cast<int>((p.M + kBM - 1) / kBM);
@@ -881,17 +867,17 @@ void launch_tc(const GemmProblem& p, const CUtensorMap& ma, const CUtensorMap& m
     tp.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (uint32_t(tp.a_mn) << 15) |
                (uint32_t(tp.b_mn) << 16) | (uint32_t(BN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
     const int grid = std::min(tp.num_tiles, num_sms(dev));
-    gemm_tc_kernel<T, BN><<<grid, kThreads, smem, stream>>>(ma, mb, tp);
+    kern<<<grid, kThreads, smem, stream>>>(ma, mb, tp);
     check_launch("gemm_tc");
 }
 
-template <typename T>
+template <typename T, bool A_MN, bool B_MN, bool BATCHED>
 void launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, TcParams& tp, int dev, cudaStream_t stream) {
     constexpr size_t smem = tc2_smem_bytes<T>();
+    auto kern = gemm_tc2_kernel<T, A_MN, B_MN, BATCHED>;
     static bool configured[64] = {};
     if (!configured[dev]) {
-        TPB_CUDA(cudaFuncSetAttribute(gemm_tc2_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(smem)));
+        TPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
         configured[dev] = true;
     }
     tp.m_tiles = (tp.M + kPairBM - 1) / kPairBM;
@@ -907,8 +893,41 @@ void launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, TcParams& tp, int 
     int group_m = static_cast<int>(std::max<int64_t>(1, (int64_t(32) << 20) / std::max<int64_t>(panel, 1)));
     group_m = std::min(group_m, tp.m_tiles);
     const int clusters = std::min(tp.num_tiles, num_sms(dev) / 2);
-    gemm_tc2_kernel<T><<<2 * clusters, kThreads, smem, stream>>>(ma, mb, tp, group_m);
+    kern<<<2 * clusters, kThreads, smem, stream>>>(ma, mb, tp, group_m);
     check_launch("gemm_tc2");
+}
+
+// The kernel instance for the operands' layouts and batching.  fp32 (TF32)
+// operands always arrive K-major, so only that instance is built for them.
+template <typename T, bool A_MN, bool B_MN, bool BATCHED>
+void launch_layout(bool pair, int bn, const GemmProblem& p, const CUtensorMap& ma, const CUtensorMap& mb,
+                   TcParams& tp, int dev, cudaStream_t stream) {
+    if (pair) launch_tc2<T, A_MN, B_MN, BATCHED>(ma, mb, tp, dev, stream);
+    else if (bn == 256) launch_tc<T, 256, A_MN, B_MN, BATCHED>(p, ma, mb, tp, dev, stream);
+    else launch_tc<T, 128, A_MN, B_MN, BATCHED>(p, ma, mb, tp, dev, stream);
+}
+
+template <typename T>
+void launch_any(bool pair, int bn, const GemmProblem& p, const CUtensorMap& ma, const CUtensorMap& mb,
+                TcParams& tp, int dev, cudaStream_t stream) {
+    const bool bt = tp.batched != 0;
+    if constexpr (std::is_same<T, float>::value) {
+        TPB_CHECK(!tp.a_mn && !tp.b_mn, "gemm: TF32 operands must be K-major");
+        if (bt) launch_layout<T, false, false, true>(pair, bn, p, ma, mb, tp, dev, stream);
+        else launch_layout<T, false, false, false>(pair, bn, p, ma, mb, tp, dev, stream);
+    } else {
+        const int code = (tp.a_mn ? 4 : 0) | (tp.b_mn ? 2 : 0) | (bt ? 1 : 0);
+        switch (code) {
+            case 0: launch_layout<T, false, false, false>(pair, bn, p, ma, mb, tp, dev, stream); break;
+            case 1: launch_layout<T, false, false, true>(pair, bn, p, ma, mb, tp, dev, stream); break;
+            case 2: launch_layout<T, false, true, false>(pair, bn, p, ma, mb, tp, dev, stream); break;
+            case 3: launch_layout<T, false, true, true>(pair, bn, p, ma, mb, tp, dev, stream); break;
+            case 4: launch_layout<T, true, false, false>(pair, bn, p, ma, mb, tp, dev, stream); break;
+            case 5: launch_layout<T, true, false, true>(pair, bn, p, ma, mb, tp, dev, stream); break;
+            case 6: launch_layout<T, true, true, false>(pair, bn, p, ma, mb, tp, dev, stream); break;
+            default: launch_layout<T, true, true, true>(pair, bn, p, ma, mb, tp, dev, stream); break;
+        }
+    }
 }
 
 // Which kernel: the CTA-pair kernel for problems with at least one full
@@ -989,11 +1008,12 @@ bool gemm_tc_typed(const GemmProblem& p_in, int dev, cudaStream_t stream, CUtens
     const bool pair = use_pair_kernel(p);
     const int bn = pair ? 128 : choose_bn(p.M, p.N, p.batch, sms);  // B rows staged per CTA
     constexpr int kEPR = 128 / es;
-    // A box: K-major 64 x 128 rows; M-major 64 (M) x 64 (K) chunks.  B box:
-    // K-major 64 x bn rows; N-major 64 x 64 chunks.
-    const CUtensorMap ma = a_k ? make_map(p.a, type, es, p.K, p.M, p.sa_m, p.batch, p.sa_b, kBM)
+    // Boxes: K-major operands kEPR (K) x kBoxRows rows (a stage takes 128 /
+    // kBoxRows, or bn / kBoxRows, of them); MN-major operands kEPR (MN) x kEPR
+    // (K) chunks.
+    const CUtensorMap ma = a_k ? make_map(p.a, type, es, p.K, p.M, p.sa_m, p.batch, p.sa_b, kBoxRows)
                                : make_map(p.a, type, es, p.M, p.K, p.sa_k, p.batch, p.sa_b, kEPR);
-    const CUtensorMap mb = b_k ? make_map(p.b, type, es, p.K, p.N, p.sb_n, p.batch, p.sb_b, bn)
+    const CUtensorMap mb = b_k ? make_map(p.b, type, es, p.K, p.N, p.sb_n, p.batch, p.sb_b, kBoxRows)
                                : make_map(p.b, type, es, p.N, p.K, p.sb_k, p.batch, p.sb_b, kEPR);
     TcParams tp{};
     tp.M = static_cast<int>(p.M);
@@ -1015,9 +1035,7 @@ bool gemm_tc_typed(const GemmProblem& p_in, int dev, cudaStream_t stream, CUtens
     tp.beta = static_cast<float>(p.beta);
     tp.vec_store = aligned16(p.c) && (p.sc_m * es) % 16 == 0 && (p.batch == 1 || (p.sc_b * es) % 16 == 0);
     tp.err = device_error_word(dev);
-    if (pair) launch_tc2<T>(ma, mb, tp, dev, stream);
-    else if (bn == 256) launch_tc<T, 256>(p, ma, mb, tp, dev, stream);
-    else launch_tc<T, 128>(p, ma, mb, tp, dev, stream);
+    launch_any<T>(pair, bn, p, ma, mb, tp, dev, stream);
     return true;
 }
 
