@@ -456,7 +456,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     e2e_value = samples / (e2e_ms * 1e-3)
     gemm_flops = 2.0 * PER_RANK_BATCH * D_IN * D_HIDDEN
     achieved = gemm_flops / (gemm_avg_ms * 1e-3) / 1e12
-    traffic = profile_figure("gemm_tc_mlp_8192x16384x4096.md", "dram_bytes_per_launch")
+    traffic = profile_figure("gemm_tc2_mlp_8192x16384x4096.md", "dram_bytes_per_launch")
 
     line = None
     if rank == 0:
@@ -472,7 +472,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             "steps_per_s": round(1000.0 / ms, 2),
             "step_tflops": round(model.flops_per_step() / (ms * 1e-3) / 1e12, 1),
             "train_loss": loss_value,
-            "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05, bf16 -> fp32)",
+            "roofline": {"bound": "tensor", "kernel": "gemm_tc2_kernel (tcgen05 cta_group::2, bf16 -> fp32)",
                          "achieved": round(achieved, 1), "peak": bf16_sustained, "unit": "TFLOP/s",
                          "frac": round(achieved / bf16_sustained, 3), "traffic": traffic,
                          "peak_kind": f"{peak_kind} sustained bf16 (kernel timed inside a long step)",
