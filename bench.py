@@ -377,7 +377,10 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     pg = D.create(_PrefixStore("nccl_b200", host.store), rank, world, device=local, timeout_s=300) \
         if world > 1 else None
 
-    cfg = MLPConfig(d_in=D_IN, d_hidden=D_HIDDEN, batch=PER_RANK_BATCH)
+    # TPB200_DW1_SLICES overrides how many slices the last gradient bucket is
+    # exchanged in (A/B measurements; the default is MLPConfig's).
+    slices = int(os.environ.get("TPB200_DW1_SLICES", MLPConfig.dw1_slices))
+    cfg = MLPConfig(d_in=D_IN, d_hidden=D_HIDDEN, batch=PER_RANK_BATCH, dw1_slices=slices)
     model = DataParallelMLP(cfg, device=local, pg=pg, host_params=init_params_host(cfg, seed=0))
     xh, th = make_batch_host(cfg, seed=rank)
     x, t = ops.to_device(xh), ops.to_device(th)

@@ -98,6 +98,22 @@ int tp_b200_take_device_error(int dev);
  * devices, all threads).  No reference counterpart: lets a benchmark state
  * how many of its kernels ran inside a timed region. */
 int64_t tp_b200_launch_count(void);
+/* Replayed recordings add the kernels one replay runs. */
+
+/* ------------------------------------------------------------------------
+ * Recording and replay (replaces tensorplay_mlu/csrc/GraphCapture.cpp:69-130,
+ * tp_mlu_capture_*).  CUDA stream capture of the calling thread's current
+ * stream of `dev` (tp_b200_set_stream; a created stream, not the default
+ * one) into a graph, instantiated at the end and launched by invoke on the
+ * thread's current stream.  Blocks the caching allocator hands out while
+ * recording are held until reset.  One recording at a time.
+ * ---------------------------------------------------------------------- */
+int tp_b200_capture_ready(void);                 /* 1 when a recording can be invoked */
+void tp_b200_capture_stats(int64_t out[2]);      /* blocks handed out while recording, blocks held */
+int tp_b200_capture_begin(int dev);
+int tp_b200_capture_end(int dev);
+int tp_b200_capture_invoke(int dev);
+int tp_b200_capture_reset(void);
 
 /* ------------------------------------------------------------------------
  * Caching allocator (replaces tensorplay_mlu/csrc/MLUAllocator.cpp:61-237 and

@@ -96,6 +96,12 @@ _SIGNATURES = {
     "tp_b200_last_error": ([], ctypes.c_char_p),
     "tp_b200_take_device_error": ([_I], _I),
     "tp_b200_launch_count": ([], _I64),
+    "tp_b200_capture_ready": ([], _I),
+    "tp_b200_capture_stats": ([ctypes.POINTER(ctypes.c_int64)], None),
+    "tp_b200_capture_begin": ([_I], _I),
+    "tp_b200_capture_end": ([_I], _I),
+    "tp_b200_capture_invoke": ([_I], _I),
+    "tp_b200_capture_reset": ([], _I),
     "tp_b200_malloc": ([_SZ, _I, _P], _P),
     "tp_b200_free": ([_P, _SZ, _I, _P], None),
     "tp_b200_memory_stats": ([_I, ctypes.POINTER(_I64)], None),

@@ -86,6 +86,12 @@ void cache_free(void* ptr, int dev, cudaStream_t stream) {
     instance().release(ptr, stream);
 }
 
+void capture_holding(bool on) { instance().set_capture_holding(on); }
+void freeze_capture_blocks() { instance().freeze_capture_blocks(); }
+void drop_capture_blocks() { instance().drop_capture_blocks(); }
+int64_t capture_allocations() { return instance().capture_allocations(); }
+int64_t capture_blocks() { return instance().capture_blocks(); }
+
 }  // namespace tpb
 
 using namespace tpb;

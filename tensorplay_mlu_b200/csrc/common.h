@@ -34,6 +34,7 @@ void set_last_error(const std::string& message);
     do {                                                                            \
         const cudaError_t tpb_status_ = (expr);                                     \
         if (tpb_status_ != cudaSuccess) {                                           \
+            (void)cudaGetLastError(); /* a later launch check must not see it */    \
             throw ::tpb::Error(::tpb::format("CUDA error: %s (%s) at %s:%d",        \
                                              cudaGetErrorString(tpb_status_), #expr, \
                                              __FILE__, __LINE__));                  \
@@ -140,8 +141,17 @@ private:
 void* cache_alloc(size_t nbytes, int dev, cudaStream_t stream);
 void cache_free(void* ptr, int dev, cudaStream_t stream);
 
+// Recording hooks of the caching allocator (graph.cpp drives them).
+void capture_holding(bool on);
+void freeze_capture_blocks();
+void drop_capture_blocks();
+int64_t capture_allocations();
+int64_t capture_blocks();
+
 // Kernels launched by this library since load (tp_b200_launch_count).
 void count_launch();
+void count_launches(int64_t n);
+void uncount_launches(int64_t n);
 
 // Launch-time check for the last kernel launch.
 inline void check_launch(const char* what) {

@@ -36,6 +36,8 @@ std::atomic<int64_t> g_launches{0};
 }  // namespace
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+void count_launches(int64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+void uncount_launches(int64_t n) { g_launches.fetch_sub(n, std::memory_order_relaxed); }
 
 std::string format(const char* fmt, ...) {
     char buf[1024];

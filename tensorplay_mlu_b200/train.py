@@ -37,6 +37,10 @@ class MLPConfig:
     batch: int = 8192
     lr: float = 1e-3
     dtype: torch.dtype = torch.bfloat16
+    # Data-parallel: the last gradient bucket (dW1, db1) is produced and
+    # all-reduced in this many row slices, so each slice's exchange overlaps
+    # the next slice's GEMM.
+    dw1_slices: int = 1
 
 
 def init_params_host(cfg: MLPConfig, seed: int = 0):
@@ -148,20 +152,50 @@ class DataParallelMLP:
             work_a = self._allreduce_async(self.bucket_a, ev)
         d_a = self._timed(ops.mm, d_out, self.w2)
         d_h = ops.gelu_backward(d_a, h)
-        self._timed(self._mm_into, self.dw1, d_h.t(), x)
+        if self.comm_stream is None:
+            self._timed(self._mm_into, self.dw1, d_h.t(), x)
+            self._colsum_into(self.db1, d_h)
+            # SGD: p += -lr * g
+            for p, g in zip(self.params(), self.grads()):
+                ops.add__Tensor(p, g, alpha=-cfg.lr)
+            return loss
+        # Bucket B in row slices of dW1 (db1 travels with the last slice);
+        # each slice's SUM all-reduce starts once its GEMM is done.
         self._colsum_into(self.db1, d_h)
-        scale = -cfg.lr
-        if self.comm_stream is not None:
+        works_b = self._dw1_sliced(d_h, x)
+        # SGD: p += (-lr / world) * g_sum, W2/b2 as soon as bucket A is in.
+        scale = -cfg.lr / self.world
+        work_a.wait()
+        ops.add__Tensor(self.w2, self.dw2, alpha=scale)
+        ops.add__Tensor(self.b2, self.db2, alpha=scale)
+        for w in works_b:
+            w.wait()
+        ops.add__Tensor(self.w1, self.dw1, alpha=scale)
+        ops.add__Tensor(self.b1, self.db1, alpha=scale)
+        return loss
+
+    def _dw1_sliced(self, d_h, x):
+        """dW1 = d_h^T x as `dw1_slices` row slices (one timed GEMM region),
+        each slice's all-reduce issued as soon as the slice is written."""
+        H, D = self.cfg.d_hidden, self.cfg.d_in
+        n = max(1, int(self.cfg.dw1_slices))
+        bounds = [(H * i // n) // 8 * 8 for i in range(n)] + [H]  # 16-byte-aligned column offsets of d_h
+        works = []
+        start = end = None
+        if self.gemm_events is not None:
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+        for i in range(n):
+            r0, r1 = bounds[i], bounds[i + 1]
+            self._mm_into(self.dw1[r0:r1], d_h[:, r0:r1].t(), x)
             ev = torch.cuda.Event()
             ev.record()
-            work_b = self._allreduce_async(self.bucket_b, ev)
-            work_a.wait()
-            work_b.wait()
-            scale = -cfg.lr / self.world
-        # SGD: p += (-lr / world) * g_sum
-        for p, g in zip(self.params(), self.grads()):
-            ops.add__Tensor(p, g, alpha=scale)
-        return loss
+            length = (r1 - r0) * D if i < n - 1 else self.bucket_b.numel() - r0 * D  # + db1
+            works.append(self._allreduce_async(self.bucket_b.narrow(0, r0 * D, length), ev))
+        if start is not None:
+            end.record()
+            self.gemm_events.append((start, end))
+        return works
 
     def flops_per_step(self) -> float:
         """Five GEMMs of 2 * B * D * H each (forward 2, backward 3, no dX)."""

@@ -65,4 +65,9 @@ int64_t fake_cross_waits() { return g_alloc->cross_stream_waits(); }
 int64_t fake_device_syncs() { return g_syncs; }
 int64_t fake_used() { return g_used; }
 size_t fake_round(size_t n) { return tpb::round_request(n); }
+void fake_capture_holding(int on) { g_alloc->set_capture_holding(on != 0); }
+void fake_capture_freeze() { g_alloc->freeze_capture_blocks(); }
+void fake_capture_drop() { g_alloc->drop_capture_blocks(); }
+int64_t fake_capture_allocations() { return g_alloc->capture_allocations(); }
+int64_t fake_capture_blocks() { return g_alloc->capture_blocks(); }
 }

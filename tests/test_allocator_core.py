@@ -27,7 +27,9 @@ def fake(tmp_path_factory):
     lib.fake_free.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
     lib.fake_stats.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int64)]
     lib.fake_reset.argtypes = [ctypes.c_int64]
-    for name in ("fake_raw_allocs", "fake_cross_waits", "fake_device_syncs", "fake_used"):
+    lib.fake_capture_holding.argtypes = [ctypes.c_int]
+    for name in ("fake_raw_allocs", "fake_cross_waits", "fake_device_syncs", "fake_used",
+                 "fake_capture_allocations", "fake_capture_blocks"):
         getattr(lib, name).restype = ctypes.c_int64
     lib.fake_round.restype = ctypes.c_size_t
     lib.fake_round.argtypes = [ctypes.c_size_t]
@@ -114,3 +116,52 @@ def test_devices_are_separate(fake):
     p = fake.fake_alloc(2 * MiB, 1, S1)
     assert stats(fake, 1)[0] == 2 * MiB and stats(fake, 0)[0] == 0
     fake.fake_free(p, S1)
+
+
+def test_recording_holds_its_blocks_until_dropped(fake):
+    """Stream capture (MLUAllocator.cpp:130-190): blocks handed out while
+    recording are reused only inside the recording, are frozen when it ends,
+    and go back to the driver only when it is dropped."""
+    MiB = 1 << 20
+    fake.fake_reset(1 << 30)
+    before = fake.fake_alloc(2 * MiB, 0, S1)       # allocated before the recording
+    fake.fake_free(before, S1)                      # cached; its event is pending
+    fake.fake_capture_holding(1)
+    a = fake.fake_alloc(2 * MiB, 0, S1)             # pending event: not taken while recording
+    assert a != before
+    fake.fake_free(a, S1)                           # given back inside the recording...
+    b = fake.fake_alloc(2 * MiB, 0, S1)             # ...and reused by the recording itself
+    assert b == a and fake.fake_cross_waits() == 0
+    c = fake.fake_alloc(4 * MiB, 0, S1)
+    assert fake.fake_capture_allocations() == 3
+    fake.fake_free(c, S1)
+    fake.fake_capture_holding(0)
+    fake.fake_capture_freeze()                      # c's block is now held
+    assert fake.fake_capture_blocks() == 1
+    d = fake.fake_alloc(4 * MiB, 0, S1)             # the held block is not handed out again
+    assert d != c
+    fake.fake_free(d, S1)
+    fake.fake_free(b, S1)                           # a block the recording uses, freed later: held
+    assert fake.fake_capture_blocks() == 2
+    reserved = stats(fake)[1]
+    syncs = fake.fake_device_syncs()
+    fake.fake_capture_drop()
+    assert fake.fake_capture_blocks() == 0 and fake.fake_device_syncs() == syncs + 1
+    assert stats(fake)[1] == reserved - 6 * MiB
+    e = fake.fake_alloc(2 * MiB, 0, S1)             # the pre-recording block is back in use
+    assert e == before
+    fake.fake_free(e, S1)
+
+
+def test_block_freed_during_recording_is_held(fake):
+    """A block from before the recording that the recorded work frees may
+    still be read by replays: it is held with the recording's blocks."""
+    MiB = 1 << 20
+    fake.fake_reset(1 << 30)
+    p = fake.fake_alloc(2 * MiB, 0, S1)
+    fake.fake_capture_holding(1)
+    fake.fake_free(p, S1)
+    fake.fake_capture_holding(0)
+    fake.fake_capture_freeze()
+    assert fake.fake_capture_blocks() == 1
+    assert fake.fake_alloc(2 * MiB, 0, S1) != p
