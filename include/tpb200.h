@@ -101,6 +101,32 @@ int64_t tp_b200_launch_count(void);
 /* Replayed recordings add the kernels one replay runs. */
 
 /* ------------------------------------------------------------------------
+ * Normalisation and loss (replaces tensorplay_mlu/csrc/NNKernels.cpp:59-161,
+ * native_layer_norm(_backward), and :304-397, nll_loss(_backward)).
+ * layer_norm: contiguous x of rows x normalized_numel; mean / rstd flat over
+ * the rows in fp32 (fp64 for fp64 input); weight / bias / dx / dweight /
+ * dbias may be NULL (absent / not wanted).  nll_loss: (N, C) input, (N)
+ * int64 or int32 targets, optional (C) weight; reduction 0 none, 1 mean,
+ * 2 sum; `out` is (N) for none, one element otherwise; total_weight one
+ * element (0 for none).  A target outside [0, C) other than ignore_index
+ * sets the device error word (tp_b200_take_device_error) and counts as
+ * ignored.
+ * ---------------------------------------------------------------------- */
+int tp_b200_layer_norm(const tpb_tensor* y, const tpb_tensor* mean, const tpb_tensor* rstd,
+                       const tpb_tensor* x, const tpb_tensor* weight, const tpb_tensor* bias,
+                       int64_t normalized_numel, double eps, void* stream);
+int tp_b200_layer_norm_backward(const tpb_tensor* dx, const tpb_tensor* dweight,
+                                const tpb_tensor* dbias, const tpb_tensor* dy, const tpb_tensor* x,
+                                const tpb_tensor* mean, const tpb_tensor* rstd,
+                                const tpb_tensor* weight, int64_t normalized_numel, void* stream);
+int tp_b200_nll_loss(const tpb_tensor* out, const tpb_tensor* total_weight, const tpb_tensor* x,
+                     const tpb_tensor* target, const tpb_tensor* weight, int reduction,
+                     int64_t ignore_index, void* stream);
+int tp_b200_nll_loss_backward(const tpb_tensor* dx, const tpb_tensor* dy, const tpb_tensor* target,
+                              const tpb_tensor* weight, const tpb_tensor* total_weight, int reduction,
+                              int64_t ignore_index, void* stream);
+
+/* ------------------------------------------------------------------------
  * Recording and replay (replaces tensorplay_mlu/csrc/GraphCapture.cpp:69-130,
  * tp_mlu_capture_*).  CUDA stream capture of the calling thread's current
  * stream of `dev` (tp_b200_set_stream; a created stream, not the default
@@ -114,6 +140,20 @@ int tp_b200_capture_begin(int dev);
 int tp_b200_capture_end(int dev);
 int tp_b200_capture_invoke(int dev);
 int tp_b200_capture_reset(void);
+
+/* ------------------------------------------------------------------------
+ * Device timer for the profiler (replaces tensorplay_mlu/csrc/MLUProfiler.cpp:
+ * 20-80, the prof::DeviceTimerHooks TensorPlay calls around each operation).
+ * record() places a pooled timing event on the device's current library
+ * stream; elapsed_ms() waits for `end` and returns 0 on success; release()
+ * returns an event to the pool.  tp_b200_timer_pooled has no reference
+ * counterpart (events the pool holds; for tests).
+ * ---------------------------------------------------------------------- */
+int tp_b200_timer_current_device(void);
+void* tp_b200_timer_record(int dev);
+int tp_b200_timer_elapsed_ms(void* start, void* end, float* ms);
+void tp_b200_timer_release(void* event);
+int64_t tp_b200_timer_pooled(void);
 
 /* ------------------------------------------------------------------------
  * Caching allocator (replaces tensorplay_mlu/csrc/MLUAllocator.cpp:61-237 and

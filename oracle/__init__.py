@@ -87,6 +87,10 @@ def lib() -> ctypes.CDLL:
             "orc_softmax": [I, T, T, I],
             "orc_softmax_backward": [I, T, T, T, I],
             "orc_gemm": [T, T, T, T, D, D, I],
+            "orc_layer_norm": [T, T, T, T, T, T, I64, D],
+            "orc_layer_norm_backward": [T, T, T, T, T, T, T, T, I64],
+            "orc_nll_loss": [T, T, T, T, T, I, I64],
+            "orc_nll_loss_backward": [T, T, T, T, T, I, I64],
             "orc_gemm_sampled": [ctypes.c_void_p, ctypes.c_void_p, I64, T, T, T, D, D, I],
             "orc_mlp_step": [I, I, I, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float,
@@ -212,3 +216,58 @@ def mlp_step(x, t, w1, b1, w2, b2, lr: float) -> float:
 
 def num_threads() -> int:
     return lib().orc_num_threads()
+
+
+# ---------------------------------------------------------------------- NN
+
+def _stats_dtype(dtype):
+    return torch.float64 if dtype == torch.float64 else torch.float32
+
+
+def _numel(shape):
+    n = 1
+    for s in shape:
+        n *= int(s)
+    return n
+
+
+def layer_norm(x: torch.Tensor, normalized_shape, w=None, b=None, eps: float = 1e-5):
+    """(y, mean, rstd) of native_layer_norm; mean / rstd flat over the rows."""
+    x = x.contiguous()
+    D = _numel(normalized_shape)
+    rows = x.numel() // D
+    y = torch.empty(x.shape, dtype=x.dtype)
+    mean = torch.empty([rows], dtype=_stats_dtype(x.dtype))
+    rstd = torch.empty([rows], dtype=_stats_dtype(x.dtype))
+    _ok(lib().orc_layer_norm(_d(y), _d(mean), _d(rstd), _d(x), _d(w.contiguous()) if w is not None else None,
+                             _d(b.contiguous()) if b is not None else None, D, float(eps)), "layer_norm")
+    return y, mean, rstd
+
+
+def layer_norm_backward(dy, x, normalized_shape, mean, rstd, w=None):
+    """(dx, dweight, dbias) of native_layer_norm_backward."""
+    x, dy = x.contiguous(), dy.contiguous()
+    D = _numel(normalized_shape)
+    dx = torch.empty(x.shape, dtype=x.dtype)
+    dw = torch.empty(list(normalized_shape), dtype=x.dtype)
+    db = torch.empty(list(normalized_shape), dtype=x.dtype)
+    _ok(lib().orc_layer_norm_backward(_d(dx), _d(dw), _d(db), _d(dy), _d(x), _d(mean.contiguous()),
+                                      _d(rstd.contiguous()), _d(w.contiguous()) if w is not None else None, D),
+        "layer_norm_backward")
+    return dx, dw, db
+
+
+def nll_loss(x: torch.Tensor, target: torch.Tensor, w=None, reduction: int = 1, ignore_index: int = -100):
+    """(output, total_weight) of nll_loss."""
+    out = torch.empty([x.shape[0]] if reduction == 0 else [], dtype=x.dtype)
+    total = torch.empty([], dtype=x.dtype)
+    _ok(lib().orc_nll_loss(_d(out), _d(total), _d(x), _d(target), _d(w) if w is not None else None,
+                           int(reduction), int(ignore_index)), "nll_loss")
+    return out, total
+
+
+def nll_loss_backward(dy, x, target, w, reduction, ignore_index, total):
+    dx = torch.empty(x.shape, dtype=x.dtype)
+    _ok(lib().orc_nll_loss_backward(_d(dx), _d(dy.contiguous()), _d(target), _d(w) if w is not None else None,
+                                    _d(total), int(reduction), int(ignore_index)), "nll_loss_backward")
+    return dx

@@ -492,6 +492,128 @@ int orc_softmax_backward(int log_, const tpb_tensor* dx, const tpb_tensor* dy, c
     return 0;
 }
 
+/* ------------------------------------------------------------------- NN -- */
+
+/* native_layer_norm (tensorplay_mlu/csrc/NNKernels.cpp:59-107, the ATen
+ * schema it registers): contiguous rows of D elements; mean, biased
+ * variance, rstd = 1 / sqrt(var + eps), y = (x - mean) * rstd * w + b (w, b
+ * NULL: 1, 0).  mean / rstd are stored per row. */
+int orc_layer_norm(const tpb_tensor* y, const tpb_tensor* mean, const tpb_tensor* rstd, const tpb_tensor* x,
+                   const tpb_tensor* w, const tpb_tensor* b, int64_t D, double eps) {
+    const int64_t rows = numel(x) / D;
+#pragma omp parallel for schedule(static) if (rows > 16)
+    for (int64_t r = 0; r < rows; ++r) {
+        double m = 0.0;
+        for (int64_t j = 0; j < D; ++j) m += loadf(x, r * D + j);
+        m /= (double)D;
+        double v = 0.0;
+        for (int64_t j = 0; j < D; ++j) {
+            const double d = loadf(x, r * D + j) - m;
+            v += d * d;
+        }
+        v /= (double)D;
+        const double rs = 1.0 / sqrt(v + eps);
+        storef(mean, r, m);
+        storef(rstd, r, rs);
+        for (int64_t j = 0; j < D; ++j) {
+            double t = (loadf(x, r * D + j) - m) * rs;
+            if (w) t *= loadf(w, j);
+            if (b) t += loadf(b, j);
+            storef(y, r * D + j, t);
+        }
+    }
+    return 0;
+}
+
+/* native_layer_norm_backward (NNKernels.cpp:109-161) with the forward's
+ * mean / rstd: g = dy * w, xhat = (x - mean) * rstd,
+ * dx = rstd * (g - mean_j(g) - xhat * mean_j(g * xhat)),
+ * dw_j = sum_r dy * xhat, db_j = sum_r dy.  Outputs may be NULL. */
+int orc_layer_norm_backward(const tpb_tensor* dx, const tpb_tensor* dw, const tpb_tensor* db,
+                            const tpb_tensor* dy, const tpb_tensor* x, const tpb_tensor* mean,
+                            const tpb_tensor* rstd, const tpb_tensor* w, int64_t D) {
+    const int64_t rows = numel(x) / D;
+    if (dx) {
+#pragma omp parallel for schedule(static) if (rows > 16)
+        for (int64_t r = 0; r < rows; ++r) {
+            const double m = loadf(mean, r), rs = loadf(rstd, r);
+            double s1 = 0.0, s2 = 0.0;
+            for (int64_t j = 0; j < D; ++j) {
+                const double g = loadf(dy, r * D + j) * (w ? loadf(w, j) : 1.0);
+                s1 += g;
+                s2 += g * (loadf(x, r * D + j) - m) * rs;
+            }
+            s1 /= (double)D;
+            s2 /= (double)D;
+            for (int64_t j = 0; j < D; ++j) {
+                const double g = loadf(dy, r * D + j) * (w ? loadf(w, j) : 1.0);
+                const double xh = (loadf(x, r * D + j) - m) * rs;
+                storef(dx, r * D + j, rs * (g - s1 - xh * s2));
+            }
+        }
+    }
+    if (dw || db) {
+#pragma omp parallel for schedule(static) if (D > 16)
+        for (int64_t j = 0; j < D; ++j) {
+            double sw = 0.0, sb = 0.0;
+            for (int64_t r = 0; r < rows; ++r) {
+                const double g = loadf(dy, r * D + j);
+                sw += g * (loadf(x, r * D + j) - loadf(mean, r)) * loadf(rstd, r);
+                sb += g;
+            }
+            if (dw) storef(dw, j, sw);
+            if (db) storef(db, j, sb);
+        }
+    }
+    return 0;
+}
+
+/* nll_loss (NNKernels.cpp:322-360, ATen nll_loss_forward semantics): x is
+ * (N, C) log-probabilities, target (N) classes, optional weight (C).
+ * out_i = -w[t_i] * x[i, t_i], 0 where t_i == ignore; total = sum of w[t_i]
+ * over the samples not ignored; reduction 0: per sample (total 0),
+ * 1: sum / total, 2: sum.  Returns -1 for a target outside [0, C). */
+int orc_nll_loss(const tpb_tensor* out, const tpb_tensor* total, const tpb_tensor* x, const tpb_tensor* target,
+                 const tpb_tensor* w, int reduction, int64_t ignore) {
+    const int64_t N = x->sizes[0], C = x->sizes[1];
+    double loss = 0.0, wsum = 0.0;
+    for (int64_t i = 0; i < N; ++i) {
+        const int64_t t = loadi(target, i * target->strides[0]);
+        double li = 0.0;
+        if (t != ignore) {
+            if (t < 0 || t >= C) return -1;
+            const double wt = w ? loadf(w, t) : 1.0;
+            li = -wt * loadf(x, i * x->strides[0] + t * x->strides[1]);
+            wsum += wt;
+        }
+        if (reduction == 0) storef(out, i, li);
+        else loss += li;
+    }
+    if (reduction == 0) storef(total, 0, 0.0);
+    else {
+        storef(out, 0, reduction == 1 ? loss / wsum : loss);
+        storef(total, 0, wsum);
+    }
+    return 0;
+}
+
+/* nll_loss_backward (NNKernels.cpp:362-397): dx zero except
+ * dx[i, t_i] = -w[t_i] * g with g = dy_i (none), dy (sum), dy / total (mean). */
+int orc_nll_loss_backward(const tpb_tensor* dx, const tpb_tensor* dy, const tpb_tensor* target,
+                          const tpb_tensor* w, const tpb_tensor* total, int reduction, int64_t ignore) {
+    const int64_t N = dx->sizes[0], C = dx->sizes[1];
+    for (int64_t e = 0; e < N * C; ++e) storef(dx, e, 0.0);
+    for (int64_t i = 0; i < N; ++i) {
+        const int64_t t = loadi(target, i * target->strides[0]);
+        if (t == ignore) continue;
+        if (t < 0 || t >= C) return -1;
+        double g = reduction == 0 ? loadf(dy, i) : loadf(dy, 0);
+        if (reduction == 1) g /= loadf(total, 0);
+        storef(dx, i * C + t, -(w ? loadf(w, t) : 1.0) * g);
+    }
+    return 0;
+}
+
 /* ----------------------------------------------------------------- GEMM -- */
 
 /* Round an fp32 value to TF32 (10 explicit mantissa bits, nearest-even). */

@@ -102,6 +102,11 @@ _SIGNATURES = {
     "tp_b200_capture_end": ([_I], _I),
     "tp_b200_capture_invoke": ([_I], _I),
     "tp_b200_capture_reset": ([], _I),
+    "tp_b200_timer_current_device": ([], _I),
+    "tp_b200_timer_record": ([_I], _P),
+    "tp_b200_timer_elapsed_ms": ([_P, _P, ctypes.POINTER(ctypes.c_float)], _I),
+    "tp_b200_timer_release": ([_P], None),
+    "tp_b200_timer_pooled": ([], _I64),
     "tp_b200_malloc": ([_SZ, _I, _P], _P),
     "tp_b200_free": ([_P, _SZ, _I, _P], None),
     "tp_b200_memory_stats": ([_I, ctypes.POINTER(_I64)], None),
@@ -118,6 +123,10 @@ _SIGNATURES = {
     "tp_b200_softmax": ([_I, _T, _T, _I, _P], _I),
     "tp_b200_softmax_backward": ([_I, _T, _T, _T, _I, _P], _I),
     "tp_b200_gemm": ([_T, _T, _T, _T, _D, _D, _I, _P], _I),
+    "tp_b200_layer_norm": ([_T, _T, _T, _T, _T, _T, _I64, _D, _P], _I),
+    "tp_b200_layer_norm_backward": ([_T, _T, _T, _T, _T, _T, _T, _T, _I64, _P], _I),
+    "tp_b200_nll_loss": ([_T, _T, _T, _T, _T, _I, _I64, _P], _I),
+    "tp_b200_nll_loss_backward": ([_T, _T, _T, _T, _T, _I, _I64, _P], _I),
     "tp_b200_nccl_last_error": ([], ctypes.c_char_p),
     "tp_b200_nccl_unique_id_bytes": ([], _I),
     "tp_b200_nccl_get_unique_id": ([_P], _I),

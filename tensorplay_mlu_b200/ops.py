@@ -809,6 +809,142 @@ def matmul(self, other):
     return out.reshape(shape)
 
 
+# ----------------------------------------------------------------------- NN
+
+def _stats_dtype(dtype: torch.dtype) -> torch.dtype:
+    """Statistics type of layer_norm (NNKernels.cpp:53-57)."""
+    return torch.float64 if dtype == torch.float64 else torch.float32
+
+
+def _optional(t):
+    return t if isinstance(t, torch.Tensor) and t.numel() > 0 else None
+
+
+def native_layer_norm(input, normalized_shape, weight=None, bias=None, eps: float = 1e-5):
+    """``native_layer_norm`` (NNKernels.cpp:59-107): (y, mean, rstd), the
+    statistics flat over the leading dimensions, in fp32 for 16-bit inputs."""
+    _require_device(input)
+    normalized_shape = [int(s) for s in normalized_shape]
+    axis = input.dim() - len(normalized_shape)
+    if not normalized_shape or axis < 0 or list(input.shape[axis:]) != normalized_shape:
+        raise RuntimeError(f"native_layer_norm: normalized_shape {normalized_shape} does not match "
+                           f"the trailing dimensions of {list(input.shape)}")
+    if not input.dtype.is_floating_point:
+        raise RuntimeError(f"native_layer_norm: expected a floating input, got {input.dtype}")
+    w, b = _optional(weight), _optional(bias)
+    for p in (w, b):
+        if p is not None:
+            _require_device(p)
+            if p.dtype != input.dtype or list(p.shape) != normalized_shape:
+                raise RuntimeError("native_layer_norm: weight / bias must have the input dtype and the normalized shape")
+    x = _dense(input)
+    outer = 1
+    for d in input.shape[:axis]:
+        outer *= int(d)
+    d_norm = 1
+    for d in normalized_shape:
+        d_norm *= d
+    y = _empty(input.shape, input.dtype, input.device)
+    sd = _stats_dtype(input.dtype)
+    mean = _empty([outer], sd, input.device)
+    rstd = _empty([outer], sd, input.device)
+    if x.numel():
+        N.check(_lib().tp_b200_layer_norm(describe(y), describe(mean), describe(rstd), describe(x),
+                                          describe(_dense(w)) if w is not None else None,
+                                          describe(_dense(b)) if b is not None else None,
+                                          int(d_norm), float(eps), _stream(x)), "native_layer_norm")
+    return y, mean, rstd
+
+
+def native_layer_norm_backward(grad_out, input, normalized_shape, mean, rstd, weight=None, bias=None,
+                               output_mask=(True, True, True)):
+    """``native_layer_norm_backward`` (NNKernels.cpp:109-161): (dx, dweight,
+    dbias), each None where ``output_mask`` says so."""
+    _require_device(grad_out, input, mean, rstd)
+    normalized_shape = [int(s) for s in normalized_shape]
+    if list(grad_out.shape) != list(input.shape):
+        raise RuntimeError("native_layer_norm_backward: grad and input shapes differ")
+    d_norm = 1
+    for d in normalized_shape:
+        d_norm *= d
+    w = _optional(weight)
+    mask = list(output_mask) + [True] * (3 - len(output_mask))
+    dx = _empty(input.shape, input.dtype, input.device) if mask[0] else None
+    dw = _empty(normalized_shape, input.dtype, input.device) if mask[1] else None
+    db = _empty(normalized_shape, input.dtype, input.device) if mask[2] else None
+    if input.numel() and (dx is not None or dw is not None or db is not None):
+        sd = _stats_dtype(input.dtype)
+        N.check(_lib().tp_b200_layer_norm_backward(
+            describe(dx) if dx is not None else None, describe(dw) if dw is not None else None,
+            describe(db) if db is not None else None, describe(_dense(_to_dtype(grad_out, input.dtype))),
+            describe(_dense(input)), describe(_dense(_to_dtype(mean, sd))), describe(_dense(_to_dtype(rstd, sd))),
+            describe(_dense(w)) if w is not None else None, int(d_norm), _stream(input)),
+            "native_layer_norm_backward")
+    elif input.numel() == 0:
+        if dw is not None:
+            fill_(dw, 0)
+        if db is not None:
+            fill_(db, 0)
+    return dx, dw, db
+
+
+def _nll_target(target):
+    _require_device(target)
+    if target.dtype not in (torch.int64, torch.int32):
+        raise RuntimeError(f"nll_loss: expected int64 or int32 targets, got {target.dtype}")
+    return _dense(target)
+
+
+def nll_loss(self, target, weight=None, reduction: int = 1, ignore_index: int = -100):
+    """``nll_loss`` (NNKernels.cpp:322-360) for (N, C) input and (N) targets:
+    (output, total_weight); reduction 0 none, 1 mean, 2 sum.  A target
+    outside [0, C) other than ignore_index sets the device error word."""
+    _require_device(self)
+    if self.dim() != 2 or target.dim() != 1 or target.shape[0] != self.shape[0]:
+        raise RuntimeError("nll_loss: expected (N, C) input and (N) targets")
+    if reduction not in (0, 1, 2):
+        raise RuntimeError(f"nll_loss: reduction must be 0, 1 or 2, got {reduction}")
+    t = _nll_target(target)
+    w = _optional(weight)
+    if w is not None:
+        _require_device(w)
+        w = _dense(_to_dtype(w, self.dtype))
+    out = _empty([self.shape[0]] if reduction == 0 else [], self.dtype, self.device)
+    total = _empty([], self.dtype, self.device)
+    N.check(_lib().tp_b200_nll_loss(describe(out), describe(total), describe(self), describe(t),
+                                    describe(w) if w is not None else None, int(reduction), int(ignore_index),
+                                    _stream(self)), "nll_loss")
+    return out, total
+
+
+def nll_loss_backward(grad_output, self, target, weight, reduction: int, ignore_index: int, total_weight):
+    """``nll_loss_backward`` (NNKernels.cpp:362-397): d input, zero except at
+    each sample's target."""
+    _require_device(grad_output, self, total_weight)
+    t = _nll_target(target)
+    w = _optional(weight)
+    if w is not None:
+        _require_device(w)
+        w = _dense(_to_dtype(w, self.dtype))
+    dx = _empty(self.shape, self.dtype, self.device)
+    if dx.numel():
+        N.check(_lib().tp_b200_nll_loss_backward(
+            describe(dx), describe(_dense(_to_dtype(grad_output, self.dtype))), describe(t),
+            describe(w) if w is not None else None, describe(_to_dtype(total_weight, self.dtype)),
+            int(reduction), int(ignore_index), _stream(self)), "nll_loss_backward")
+    return dx
+
+
+def cross_entropy(input, target, weight=None, reduction: int = 1, ignore_index: int = -100):
+    """cross_entropy over class dimension 1 of an (N, C) input, as TensorPlay
+    composes it: nll_loss(log_softmax(input, 1), target)."""
+    return nll_loss(_log_softmax(input, 1), target, weight, reduction, ignore_index)[0]
+
+
+def layer_norm(input, normalized_shape, weight=None, bias=None, eps: float = 1e-5):
+    return native_layer_norm(input, normalized_shape, weight, bias, eps)[0]
+
+
 # ---------------------------------------------------------------- registry
 
 # Schema name -> kernel, in the reference's registration order.
@@ -882,4 +1018,9 @@ KERNELS = {
     "addmm": addmm,
     "matmul": matmul,
     "linear": linear,
+    # NNKernels.cpp:399-410 (normalisation and loss)
+    "native_layer_norm": native_layer_norm,
+    "native_layer_norm_backward": native_layer_norm_backward,
+    "nll_loss": nll_loss,
+    "nll_loss_backward": nll_loss_backward,
 }

@@ -151,6 +151,44 @@ def main() -> None:
             alpha=2.0, beta=0.5)
         x, y = rand(4, 9, 6, dtype=dt), rand(4, 6, 5, dtype=dt, seed=4)
         add("gemm", f"bmm_{dt}", [x, y], torch.bmm(x, y))
+    # ---- layer_norm forward / backward (NNKernels.cpp:59-161), one case per output
+    aten = torch.ops.aten
+    for dt in float_types:
+        for shape, norm, affine in (((6, 20), [20], True), ((3, 4, 16), [4, 16], True), ((5, 33), [33], False)):
+            x = rand(*shape, dtype=dt, seed=11, scale=2.0)
+            w = rand(*norm, dtype=dt, seed=12) if affine else None
+            b = rand(*norm, dtype=dt, seed=13) if affine else None
+            y, mean, rstd = aten.native_layer_norm(x, norm, w, b, 1e-5)
+            tag = f"{'x'.join(map(str, shape))}_{dt}"
+            ins = [x] + ([w, b] if affine else [])
+            for part, out in (("y", y), ("mean", mean.reshape(-1)), ("rstd", rstd.reshape(-1))):
+                add("layer_norm", f"layer_norm_{part}_{tag}", ins, out, norm=norm, part=part, eps=1e-5)
+            dy = rand(*shape, dtype=dt, seed=14)
+            dx, dw, db = aten.native_layer_norm_backward(dy, x, norm, mean, rstd, w, b, [True, affine, affine])
+            bins = [dy, x, mean.reshape(-1).float() if dt != torch.float64 else mean.reshape(-1),
+                    rstd.reshape(-1).float() if dt != torch.float64 else rstd.reshape(-1)] + ([w] if affine else [])
+            add("layer_norm_backward", f"layer_norm_backward_dx_{tag}", bins, dx, norm=norm, part="dx")
+            if affine:
+                add("layer_norm_backward", f"layer_norm_backward_dw_{tag}", bins, dw, norm=norm, part="dw")
+                add("layer_norm_backward", f"layer_norm_backward_db_{tag}", bins, db, norm=norm, part="db")
+    # ---- nll_loss forward / backward (NNKernels.cpp:304-397), class weights and ignore_index
+    for dt in float_types:
+        x = torch.log_softmax(rand(9, 7, seed=15, scale=2.0), 1).to(dt)
+        t = torch.tensor([0, 3, 6, -100, 2, 2, 5, 1, -100], dtype=torch.int64)
+        wt = (rand(7, seed=16).abs() + 0.5).to(dt)
+        for red in (0, 1, 2):
+            for w_on in (False, True):
+                w = wt if w_on else None
+                out, total = aten.nll_loss_forward(x, t, w, red, -100)
+                tag = f"r{red}_{'w' if w_on else 'nw'}_{dt}"
+                ins = [x, t] + ([w] if w_on else [])
+                add("nll_loss", f"nll_loss_out_{tag}", ins, out, reduction=red, part="out")
+                if red != 0:
+                    add("nll_loss", f"nll_loss_total_{tag}", ins, total, reduction=red, part="total")
+                g = rand(9, dtype=dt, seed=17) if red == 0 else torch.tensor(1.5, dtype=dt)
+                dx = aten.nll_loss_backward(g, x, t, w, red, -100, total)
+                add("nll_loss_backward", f"nll_loss_backward_{tag}", [g, x, t, total] + ([w] if w_on else []), dx,
+                    reduction=red)
     # ---- casts (test_mlu.py:90-98) and round trips (:64-69): exact
     src = rand(3, 9, scale=4.0)
     for s, d in ((torch.float32, torch.float16), (torch.float16, torch.float32),

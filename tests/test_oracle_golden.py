@@ -58,6 +58,24 @@ def oracle_output(case):
         return O.gemm(ins[0], ins[1])
     if kind == "cast":
         return O.cast(ins[0], p["dtype"])
+    if kind == "layer_norm":
+        x, w, b = (ins + [None, None])[:3]
+        y, mean, rstd = O.layer_norm(x, p["norm"], w, b, p["eps"])
+        return {"y": y, "mean": mean, "rstd": rstd}[p["part"]]
+    if kind == "layer_norm_backward":
+        dy, x, mean, rstd = ins[:4]
+        w = ins[4] if len(ins) > 4 else None
+        dx, dw, db = O.layer_norm_backward(dy, x, p["norm"], mean, rstd, w)
+        return {"dx": dx, "dw": dw, "db": db}[p["part"]]
+    if kind == "nll_loss":
+        x, t = ins[:2]
+        w = ins[2] if len(ins) > 2 else None
+        out, total = O.nll_loss(x, t, w, p["reduction"], -100)
+        return {"out": out, "total": total}[p["part"]]
+    if kind == "nll_loss_backward":
+        g, x, t, total = ins[:4]
+        w = ins[4] if len(ins) > 4 else None
+        return O.nll_loss_backward(g, x, t, w, p["reduction"], -100, total)
     raise AssertionError(kind)
 
 
@@ -78,13 +96,17 @@ def test_oracle_matches_golden(case):
             scale = 4.0  # reduction order: oracle accumulates in double, PyTorch in fp32
         if case["kind"] == "reduce" and case["params"]["op"] == "sum":
             scale = 20.0
+        if case["kind"].startswith("layer_norm") or case["kind"].startswith("nll"):
+            scale = 4.0  # fp32 / 16-bit statistics and sums rounded in a different order
+        got = got.to(want.dtype) if got.dtype != want.dtype else got
         assert_close(got, want, want.dtype, scale)
 
 
 def test_golden_covers_every_family():
     kinds = {c["kind"] for c in CASES}
     assert {"binary", "scalar", "unary", "unary_backward", "reduce", "softmax", "softmax_backward",
-            "gemm", "cast", "scalar_chain"} <= kinds
+            "gemm", "cast", "scalar_chain", "layer_norm", "layer_norm_backward", "nll_loss",
+            "nll_loss_backward"} <= kinds
 
 
 def test_oracle_mlp_step_matches_torch_autograd():
