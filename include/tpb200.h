@@ -125,6 +125,44 @@ int tp_b200_nll_loss(const tpb_tensor* out, const tpb_tensor* total_weight, cons
 int tp_b200_nll_loss_backward(const tpb_tensor* dx, const tpb_tensor* dy, const tpb_tensor* target,
                               const tpb_tensor* weight, const tpb_tensor* total_weight, int reduction,
                               int64_t ignore_index, void* stream);
+/* native_dropout / native_dropout_backward (NNKernels.cpp:164-236): keep an
+ * element with probability 1 - p (uniform on 24 bits from Philox-4x32-10 at
+ * counter (element / 4 + offset), key seed) and scale it by 1 / (1 - p);
+ * `mask` (bool) records the kept elements.  masked_scale: dx = dy * mask *
+ * scale.  Contiguous operands; 0 <= p < 1 (p = 1 needs no kernel). */
+int tp_b200_dropout(const tpb_tensor* out, const tpb_tensor* mask, const tpb_tensor* x, double p,
+                    uint64_t seed, uint64_t offset, void* stream);
+int tp_b200_masked_scale(const tpb_tensor* dx, const tpb_tensor* dy, const tpb_tensor* mask, double scale,
+                         void* stream);
+
+/* ------------------------------------------------------------------------
+ * Indexing, scatter, scans, where (replaces tensorplay_mlu/csrc/
+ * IndexKernels.cpp:45-352: gather, index_select, the scatter family,
+ * cumsum / cumprod, where.self).  Index tensors are int64 or int32; negative
+ * indices count from the end; an index outside the dimension writes nothing
+ * and sets the device error word.
+ *   gather:       out (index's shape) = self[.., index, ..] along dim.
+ *   index_select: contiguous self / out, 0-d or 1-d index.
+ *   index_add:    out[.., index[l], ..] += src[.., l, ..] (contiguous).
+ *   scatter:      out (holding `self` on entry) at index along dim, over
+ *                 index's shape: mode 0 replace, 1 add, 2 multiply, 3 amax,
+ *                 4 amin, 5 mean (contiguous out); include_self 0 starts
+ *                 the landed elements from the mode's identity.
+ *   scan:         inclusive cumulative sum (product != 0: product) along
+ *                 dim; contiguous input and result of one dtype.
+ *   where:        out = cond ? a : b with broadcasting; cond bool.
+ * ---------------------------------------------------------------------- */
+int tp_b200_gather(const tpb_tensor* out, const tpb_tensor* self, const tpb_tensor* index, int dim,
+                   void* stream);
+int tp_b200_index_select(const tpb_tensor* out, const tpb_tensor* self, const tpb_tensor* index,
+                         int dim, void* stream);
+int tp_b200_index_add(const tpb_tensor* out, const tpb_tensor* src, const tpb_tensor* index, int dim,
+                      void* stream);
+int tp_b200_scatter(const tpb_tensor* out, const tpb_tensor* index, const tpb_tensor* src, int dim,
+                    int mode, int include_self, void* stream);
+int tp_b200_scan(int product, const tpb_tensor* out, const tpb_tensor* x, int dim, void* stream);
+int tp_b200_where(const tpb_tensor* out, const tpb_tensor* cond, const tpb_tensor* a,
+                  const tpb_tensor* b, void* stream);
 
 /* ------------------------------------------------------------------------
  * Recording and replay (replaces tensorplay_mlu/csrc/GraphCapture.cpp:69-130,

@@ -87,6 +87,13 @@ def lib() -> ctypes.CDLL:
             "orc_softmax": [I, T, T, I],
             "orc_softmax_backward": [I, T, T, T, I],
             "orc_gemm": [T, T, T, T, D, D, I],
+            "orc_dropout": [T, T, T, D, ctypes.c_uint64, ctypes.c_uint64],
+            "orc_gather": [T, T, T, I],
+            "orc_index_select": [T, T, T, I],
+            "orc_index_add": [T, T, T, I],
+            "orc_scatter": [T, T, T, I, I, I],
+            "orc_scan": [I, T, T, I],
+            "orc_where": [T, T, T, T],
             "orc_layer_norm": [T, T, T, T, T, T, I64, D],
             "orc_layer_norm_backward": [T, T, T, T, T, T, T, T, I64],
             "orc_nll_loss": [T, T, T, T, T, I, I64],
@@ -271,3 +278,75 @@ def nll_loss_backward(dy, x, target, w, reduction, ignore_index, total):
     _ok(lib().orc_nll_loss_backward(_d(dx), _d(dy.contiguous()), _d(target), _d(w) if w is not None else None,
                                     _d(total), int(reduction), int(ignore_index)), "nll_loss_backward")
     return dx
+
+
+# -------------------------------------------------------------------- index
+
+SCATTER_MODES = {None: 0, "add": 1, "sum": 1, "multiply": 2, "prod": 2, "amax": 3, "amin": 4, "mean": 5}
+
+
+def gather(self: torch.Tensor, dim: int, index: torch.Tensor) -> torch.Tensor:
+    out = torch.empty(index.shape, dtype=self.dtype)
+    _ok(lib().orc_gather(_d(out), _d(self), _d(index), dim % max(self.dim(), 1)), "gather")
+    return out
+
+
+def index_select(self: torch.Tensor, dim: int, index: torch.Tensor) -> torch.Tensor:
+    x = self.contiguous()
+    d = dim % max(self.dim(), 1)
+    shape = list(self.shape)
+    shape[d] = index.numel()
+    out = torch.empty(shape, dtype=self.dtype)
+    _ok(lib().orc_index_select(_d(out), _d(x), _d(index.reshape(-1)), d), "index_select")
+    return out
+
+
+def index_add_zeros(shape, dim: int, index: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
+    out = torch.zeros(shape, dtype=src.dtype)
+    _ok(lib().orc_index_add(_d(out), _d(src.contiguous()), _d(index.reshape(-1)), dim % max(len(shape), 1)),
+        "index_add")
+    return out
+
+
+def scatter(self: torch.Tensor, dim: int, index: torch.Tensor, src: torch.Tensor, reduce=None,
+            include_self: bool = True) -> torch.Tensor:
+    out = self.clone().contiguous()
+    _ok(lib().orc_scatter(_d(out), _d(index), _d(src), dim % max(self.dim(), 1), SCATTER_MODES[reduce],
+                          int(include_self)), "scatter")
+    return out
+
+
+def scan(x: torch.Tensor, dim: int, product: bool = False) -> torch.Tensor:
+    x = x.contiguous()
+    out = torch.empty(x.shape, dtype=x.dtype)
+    _ok(lib().orc_scan(int(product), _d(out), _d(x), dim % max(x.dim(), 1)), "scan")
+    return out
+
+
+def where(cond: torch.Tensor, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    out = torch.empty(torch.broadcast_shapes(cond.shape, a.shape, b.shape), dtype=a.dtype)
+    _ok(lib().orc_where(_d(out), _d(cond), _d(a), _d(b)), "where")
+    return out
+
+
+# ------------------------------------------------------------------ dropout
+
+def philox4x32_10(ctr, key):
+    """Philox-4x32-10 block for four 32-bit counter words and two key words."""
+    c = (ctypes.c_uint32 * 4)(*ctr)
+    k = (ctypes.c_uint32 * 2)(*key)
+    out = (ctypes.c_uint32 * 4)()
+    fn = lib().orc_philox4x32_10
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    fn.restype = None
+    fn(ctypes.addressof(c), ctypes.addressof(k), ctypes.addressof(out))
+    return list(out)
+
+
+def dropout(x: torch.Tensor, p: float, seed: int, offset: int = 0):
+    """(output, mask) of the device dropout kernel's element -> random-word mapping."""
+    x = x.contiguous()
+    out = torch.empty(x.shape, dtype=x.dtype)
+    mask = torch.empty(x.shape, dtype=torch.bool)
+    _ok(lib().orc_dropout(_d(out), _d(mask), _d(x), float(p), int(seed), int(offset)), "dropout")
+    return out, mask

@@ -614,6 +614,247 @@ int orc_nll_loss_backward(const tpb_tensor* dx, const tpb_tensor* dy, const tpb_
     return 0;
 }
 
+/* -------------------------------------------------------------- dropout -- */
+
+/* Philox-4x32-10 (Salmon, Moraes, Dror and Shaw, SC 2011): ten rounds, each
+ * two 32x32 -> 64-bit products (multipliers 0xD2511F53, 0xCD9E8D57) mixing
+ * the four counter words with the two key words, the key bumped by the Weyl
+ * constants 0x9E3779B9, 0xBB67AE85 between rounds. */
+void orc_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]) {
+    uint32_t c0 = ctr[0], c1 = ctr[1], c2 = ctr[2], c3 = ctr[3], k0 = key[0], k1 = key[1];
+    for (int r = 0; r < 10; ++r) {
+        const uint64_t p0 = (uint64_t)0xD2511F53u * c0, p1 = (uint64_t)0xCD9E8D57u * c2;
+        const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c1 ^ k0, n1 = (uint32_t)p1;
+        const uint32_t n2 = (uint32_t)(p0 >> 32) ^ c3 ^ k1, n3 = (uint32_t)p0;
+        c0 = n0; c1 = n1; c2 = n2; c3 = n3;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
+}
+
+/* native_dropout (NNKernels.cpp:164-196) with the element -> random word
+ * mapping of the device kernel: element e uses word e % 4 of Philox at
+ * counter (e / 4 + offset) (low / high 32 bits, then 0, 0) under key
+ * seed (low, high); keep when (word >> 8) / 2^24 >= p; out = x / (1 - p). */
+int orc_dropout(const tpb_tensor* out, const tpb_tensor* mask, const tpb_tensor* x, double p, uint64_t seed,
+                uint64_t offset) {
+    const int64_t n = numel(x);
+    const uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
+    const float scale = (float)(1.0 / (1.0 - p));
+    for (int64_t g = 0; g < (n + 3) / 4; ++g) {
+        const uint64_t c = (uint64_t)g + offset;
+        const uint32_t ctr[4] = {(uint32_t)c, (uint32_t)(c >> 32), 0u, 0u};
+        uint32_t w[4];
+        orc_philox4x32_10(ctr, key, w);
+        for (int j = 0; j < 4 && g * 4 + j < n; ++j) {
+            const int64_t e = g * 4 + j;
+            const float u = (float)(w[j] >> 8) * (1.0f / 16777216.0f);
+            const int keep = u >= (float)p;
+            storei(mask, e, keep);
+            /* x * scale rounded once into the storage type (the float scale
+             * times a float / 16-bit value is exact in double) */
+            storef(out, e, keep ? loadf(x, e) * (double)scale : 0.0);
+        }
+    }
+    return 0;
+}
+
+/* ---------------------------------------------------------------- index -- */
+
+/* Offset of the multi-index of linear position `i` over `sizes` with `st`. */
+static int64_t coords_offset(int64_t i, int nd, const int64_t* sizes, const int64_t* st, int64_t* coord) {
+    int64_t off = 0;
+    for (int d = nd - 1; d >= 0; --d) {
+        const int64_t c = sizes[d] ? i % sizes[d] : 0;
+        i = sizes[d] ? i / sizes[d] : 0;
+        if (coord) coord[d] = c;
+        off += c * st[d];
+    }
+    return off;
+}
+
+static int resolve(int64_t k, int64_t size, int64_t* out) {
+    if (k < 0) k += size;
+    if (k < 0 || k >= size) return 0;
+    *out = k;
+    return 1;
+}
+
+/* gather (IndexKernels.cpp:45-69, ATen gather): out[c] = self[c, c[dim] <- index[c]]. */
+int orc_gather(const tpb_tensor* out, const tpb_tensor* self, const tpb_tensor* index, int dim) {
+    const int nd = index->ndim;
+    const int64_t n = numel(index);
+    int64_t coord[TPB_MAX_DIMS];
+    for (int64_t i = 0; i < n; ++i) {
+        const int64_t io = coords_offset(i, nd, index->sizes, index->strides, coord);
+        const int64_t oo = coords_offset(i, nd, index->sizes, out->strides, NULL);
+        int64_t k;
+        if (!resolve(loadi(index, io), self->sizes[dim], &k)) return -1;
+        int64_t so = 0;
+        for (int d = 0; d < nd; ++d) so += (d == dim ? k : coord[d]) * self->strides[d];
+        if (is_float_dtype(self->dtype)) storef(out, oo, loadf(self, so));
+        else storei(out, oo, loadi(self, so));
+    }
+    return 0;
+}
+
+/* index_select (IndexKernels.cpp:184-209): contiguous self / out, 1-d index. */
+int orc_index_select(const tpb_tensor* out, const tpb_tensor* self, const tpb_tensor* index, int dim) {
+    int64_t outer = 1, inner = 1;
+    for (int d = 0; d < dim; ++d) outer *= self->sizes[d];
+    for (int d = dim + 1; d < self->ndim; ++d) inner *= self->sizes[d];
+    const int64_t S = self->sizes[dim], L = numel(index);
+    const int64_t ist = index->ndim ? index->strides[0] : 0;
+    for (int64_t o = 0; o < outer; ++o)
+        for (int64_t l = 0; l < L; ++l) {
+            int64_t k;
+            if (!resolve(loadi(index, l * ist), S, &k)) return -1;
+            for (int64_t j = 0; j < inner; ++j) {
+                const int64_t so = (o * S + k) * inner + j, oo = (o * L + l) * inner + j;
+                if (is_float_dtype(self->dtype)) storef(out, oo, loadf(self, so));
+                else storei(out, oo, loadi(self, so));
+            }
+        }
+    return 0;
+}
+
+/* Combine of the scatter modes: 1 add, 2 multiply, 3 amax, 4 amin (5 mean adds). */
+static double combf(int mode, double a, double b) {
+    switch (mode) {
+        case 2: return a * b;
+        case 3: return (a > b || a != a) ? a : b;
+        case 4: return (a < b || a != a) ? a : b;
+        default: return a + b;
+    }
+}
+static int64_t combi(int mode, int64_t a, int64_t b) {
+    switch (mode) {
+        case 2: return (int64_t)((uint64_t)a * (uint64_t)b);
+        case 3: return a > b ? a : b;
+        case 4: return a < b ? a : b;
+        default: return (int64_t)((uint64_t)a + (uint64_t)b);
+    }
+}
+
+/* scatter family (IndexKernels.cpp:71-115, 221-275; ATen scatter /
+ * scatter_add / scatter_reduce): `out` holds self on entry; in index order,
+ * out[c, c[dim] <- index[c]] (op)= src[c].  include_self 0 starts each landed
+ * element from the first value scattered into it; mean divides by the count
+ * (+1 with self), floor division for integers.  Values combine in double
+ * (floats) or int64 (integers) and are stored after every step, as a host
+ * loop over the storage type does. */
+int orc_scatter(const tpb_tensor* out, const tpb_tensor* index, const tpb_tensor* src, int dim, int mode,
+                int include_self) {
+    const int nd = index->ndim;
+    const int64_t n = numel(index), on = numel(out);
+    const int fl = is_float_dtype(out->dtype);
+    int64_t* count = (int64_t*)calloc((size_t)(on > 0 ? on : 1), sizeof(int64_t));
+    int64_t coord[TPB_MAX_DIMS];
+    for (int64_t i = 0; i < n; ++i) {
+        const int64_t io = coords_offset(i, nd, index->sizes, index->strides, coord);
+        const int64_t so = coords_offset(i, nd, index->sizes, src->strides, NULL);
+        int64_t k;
+        if (!resolve(loadi(index, io), out->sizes[dim], &k)) {
+            free(count);
+            return -1;
+        }
+        int64_t oo = 0, lin = 0;
+        for (int d = 0; d < nd; ++d) {
+            const int64_t c = d == dim ? k : coord[d];
+            oo += c * out->strides[d];
+            lin = lin * out->sizes[d] + c;
+        }
+        if (mode == 0) {
+            if (fl) storef(out, oo, loadf(src, so));
+            else storei(out, oo, loadi(src, so));
+            continue;
+        }
+        const int first = count[lin] == 0 && !include_self;
+        ++count[lin];
+        if (fl) storef(out, oo, first ? loadf(src, so) : combf(mode, loadf(out, oo), loadf(src, so)));
+        else storei(out, oo, first ? loadi(src, so) : combi(mode, loadi(out, oo), loadi(src, so)));
+    }
+    if (mode == 5) {
+        for (int64_t e = 0; e < on; ++e) {
+            if (count[e] == 0) continue;
+            const int64_t d = count[e] + (include_self ? 1 : 0);
+            if (fl) storef(out, e, loadf(out, e) / (double)d);
+            else {
+                const int64_t v = loadi(out, e);
+                int64_t q = v / d;
+                if ((v % d != 0) && ((v < 0) != (d < 0))) --q;
+                storei(out, e, q);
+            }
+        }
+    }
+    free(count);
+    return 0;
+}
+
+/* index_add (index_select's backward, IndexKernels.cpp:211-219): contiguous
+ * out [outer, S, inner] += src [outer, L, inner] at index[l]. */
+int orc_index_add(const tpb_tensor* out, const tpb_tensor* src, const tpb_tensor* index, int dim) {
+    int64_t outer = 1, inner = 1;
+    for (int d = 0; d < dim; ++d) outer *= out->sizes[d];
+    for (int d = dim + 1; d < out->ndim; ++d) inner *= out->sizes[d];
+    const int64_t S = out->sizes[dim], L = numel(index);
+    const int64_t ist = index->ndim ? index->strides[0] : 0;
+    for (int64_t o = 0; o < outer; ++o)
+        for (int64_t l = 0; l < L; ++l) {
+            int64_t k;
+            if (!resolve(loadi(index, l * ist), S, &k)) return -1;
+            for (int64_t j = 0; j < inner; ++j) {
+                const int64_t oo = (o * S + k) * inner + j, so = (o * L + l) * inner + j;
+                if (is_float_dtype(out->dtype)) storef(out, oo, loadf(out, oo) + loadf(src, so));
+                else storei(out, oo, combi(1, loadi(out, oo), loadi(src, so)));
+            }
+        }
+    return 0;
+}
+
+/* cumsum / cumprod (IndexKernels.cpp:123-149): inclusive, along dim, over
+ * contiguous input and result of one dtype; double / int64 accumulation. */
+int orc_scan(int product, const tpb_tensor* out, const tpb_tensor* x, int dim) {
+    int64_t outer = 1, inner = 1;
+    for (int d = 0; d < dim; ++d) outer *= x->sizes[d];
+    for (int d = dim + 1; d < x->ndim; ++d) inner *= x->sizes[d];
+    const int64_t D = x->ndim ? x->sizes[dim] : 1;
+    const int fl = is_float_dtype(x->dtype);
+    for (int64_t o = 0; o < outer; ++o)
+        for (int64_t j = 0; j < inner; ++j) {
+            double af = product ? 1.0 : 0.0;
+            int64_t ai = product ? 1 : 0;
+            for (int64_t d = 0; d < D; ++d) {
+                const int64_t e = (o * D + d) * inner + j;
+                if (fl) {
+                    af = product ? af * loadf(x, e) : af + loadf(x, e);
+                    storef(out, e, af);
+                } else {
+                    ai = combi(product ? 2 : 1, ai, loadi(x, e));
+                    storei(out, e, ai);
+                }
+            }
+        }
+    return 0;
+}
+
+/* where.self (IndexKernels.cpp:313-349): out = cond ? a : b, broadcast. */
+int orc_where(const tpb_tensor* out, const tpb_tensor* cond, const tpb_tensor* a, const tpb_tensor* b) {
+    int64_t sc[TPB_MAX_DIMS], sa[TPB_MAX_DIMS], sb[TPB_MAX_DIMS];
+    if (bstrides(cond, out, sc) || bstrides(a, out, sa) || bstrides(b, out, sb)) return -1;
+    const int64_t n = numel(out);
+    for (int64_t i = 0; i < n; ++i) {
+        const int64_t oo = offset_of(i, out->ndim, out->sizes, out->strides);
+        const int c = loadi(cond, offset_of(i, out->ndim, out->sizes, sc)) != 0;
+        const int64_t src = offset_of(i, out->ndim, out->sizes, c ? sa : sb);
+        const tpb_tensor* t = c ? a : b;
+        if (is_float_dtype(out->dtype)) storef(out, oo, loadf(t, src));
+        else storei(out, oo, loadi(t, src));
+    }
+    return 0;
+}
+
 /* ----------------------------------------------------------------- GEMM -- */
 
 /* Round an fp32 value to TF32 (10 explicit mantissa bits, nearest-even). */

@@ -123,10 +123,18 @@ _SIGNATURES = {
     "tp_b200_softmax": ([_I, _T, _T, _I, _P], _I),
     "tp_b200_softmax_backward": ([_I, _T, _T, _T, _I, _P], _I),
     "tp_b200_gemm": ([_T, _T, _T, _T, _D, _D, _I, _P], _I),
+    "tp_b200_gather": ([_T, _T, _T, _I, _P], _I),
+    "tp_b200_index_select": ([_T, _T, _T, _I, _P], _I),
+    "tp_b200_index_add": ([_T, _T, _T, _I, _P], _I),
+    "tp_b200_scatter": ([_T, _T, _T, _I, _I, _I, _P], _I),
+    "tp_b200_scan": ([_I, _T, _T, _I, _P], _I),
+    "tp_b200_where": ([_T, _T, _T, _T, _P], _I),
     "tp_b200_layer_norm": ([_T, _T, _T, _T, _T, _T, _I64, _D, _P], _I),
     "tp_b200_layer_norm_backward": ([_T, _T, _T, _T, _T, _T, _T, _T, _I64, _P], _I),
     "tp_b200_nll_loss": ([_T, _T, _T, _T, _T, _I, _I64, _P], _I),
     "tp_b200_nll_loss_backward": ([_T, _T, _T, _T, _T, _I, _I64, _P], _I),
+    "tp_b200_dropout": ([_T, _T, _T, _D, ctypes.c_uint64, ctypes.c_uint64, _P], _I),
+    "tp_b200_masked_scale": ([_T, _T, _T, _D, _P], _I),
     "tp_b200_nccl_last_error": ([], ctypes.c_char_p),
     "tp_b200_nccl_unique_id_bytes": ([], _I),
     "tp_b200_nccl_get_unique_id": ([_P], _I),

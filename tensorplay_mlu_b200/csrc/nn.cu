@@ -315,6 +315,67 @@ __global__ void __launch_bounds__(kThreads) nll_backward(T* __restrict__ dx, con
     }
 }
 
+// -------------------------------------------------------------- dropout --
+
+// Philox-4x32-10, the counter-based generator of Salmon, Moraes, Dror and
+// Shaw, "Parallel random numbers: as easy as 1, 2, 3" (SC 2011): ten rounds
+// of two 32x32 -> 64-bit products mixing a 128-bit counter under a 64-bit key
+// bumped by the Weyl constants each round.  Element e of a launch draws
+// word e % 4 of the block for counter (e / 4 + offset, 0, 0, 0).
+struct Philox4 {
+    uint32_t v[4];
+};
+
+__device__ __forceinline__ Philox4 philox4x32_10(uint64_t counter, uint64_t key) {
+    uint32_t c0 = static_cast<uint32_t>(counter), c1 = static_cast<uint32_t>(counter >> 32), c2 = 0, c3 = 0;
+    uint32_t k0 = static_cast<uint32_t>(key), k1 = static_cast<uint32_t>(key >> 32);
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        const uint32_t hi0 = __umulhi(0xD2511F53u, c0), lo0 = 0xD2511F53u * c0;
+        const uint32_t hi1 = __umulhi(0xCD9E8D57u, c2), lo1 = 0xCD9E8D57u * c2;
+        const uint32_t n0 = hi1 ^ c1 ^ k0, n1 = lo1, n2 = hi0 ^ c3 ^ k1, n3 = lo0;
+        c0 = n0;
+        c1 = n1;
+        c2 = n2;
+        c3 = n3;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    return Philox4{{c0, c1, c2, c3}};
+}
+
+// out = keep ? x / (1 - p) : 0 with keep = u >= p, u uniform in [0, 1) on
+// 24 bits; mask records keep.  Four elements per generator call.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) dropout_kernel(const T* __restrict__ x, T* __restrict__ out,
+                                                           bool* __restrict__ mask, int64_t n, float p, float scale,
+                                                           uint64_t seed, uint64_t offset) {
+    using C = typename Stat<T>::type;
+    const int64_t groups = (n + 3) / 4;
+    for (int64_t g = int64_t(blockIdx.x) * kThreads + threadIdx.x; g < groups; g += int64_t(gridDim.x) * kThreads) {
+        const Philox4 r = philox4x32_10(static_cast<uint64_t>(g) + offset, seed);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t e = g * 4 + j;
+            if (e >= n) break;
+            const float u = static_cast<float>(r.v[j] >> 8) * (1.0f / 16777216.0f);
+            const bool keep = u >= p;
+            mask[e] = keep;
+            out[e] = store_as<T>(keep ? load_as<C>(x[e]) * C(scale) : C(0));
+        }
+    }
+}
+
+// dx = dy * mask * scale.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) masked_scale_kernel(const T* __restrict__ dy, const bool* __restrict__ mask,
+                                                                T* __restrict__ dx, int64_t n, double scale) {
+    using C = typename Stat<T>::type;
+    for (int64_t e = int64_t(blockIdx.x) * kThreads + threadIdx.x; e < n; e += int64_t(gridDim.x) * kThreads) {
+        dx[e] = store_as<T>(mask[e] ? load_as<C>(dy[e]) * C(scale) : C(0));
+    }
+}
+
 // ---------------------------------------------------------- host side --
 
 const tpb_tensor* opt(const tpb_tensor* t) { return t != nullptr && t->data != nullptr ? t : nullptr; }
@@ -571,6 +632,62 @@ int tp_b200_nll_loss_backward(const tpb_tensor* dx, const tpb_tensor* dy, const 
                 check_launch("nll_loss_backward");
             });
         });
+    });
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int tp_b200_dropout(const tpb_tensor* out, const tpb_tensor* mask, const tpb_tensor* x, double p, uint64_t seed,
+                    uint64_t offset, void* stream) {
+    return guarded([&] {
+        require_dense(out, "dropout result");
+        require_dense(mask, "dropout mask");
+        require_dense(x, "dropout input");
+        TPB_CHECK(is_floating(x->dtype) && out->dtype == x->dtype, "dropout: floating input and result of one dtype");
+        TPB_CHECK(mask->dtype == TPB_BOOL, "dropout: the mask must be bool");
+        TPB_CHECK(p >= 0.0 && p < 1.0, "dropout: probability must be in [0, 1)");
+        const int64_t n = numel_of(*x);
+        TPB_CHECK(numel_of(*out) == n && numel_of(*mask) == n, "dropout: sizes differ");
+        if (n == 0) return;
+        const int dev = device_of(x->data);
+        DeviceGuard guard(dev);
+        cudaStream_t s = resolve_stream(stream, dev);
+        const unsigned grid = static_cast<unsigned>(
+            std::max<int64_t>(1, std::min<int64_t>(blocks_for((n + 3) / 4, kThreads), int64_t(num_sms(dev)) * 8)));
+        TPB_DISPATCH_FLOAT(x->dtype, "dropout", {
+            dropout_kernel<scalar_t><<<grid, kThreads, 0, s>>>(
+                static_cast<const scalar_t*>(x->data), static_cast<scalar_t*>(out->data),
+                static_cast<bool*>(mask->data), n, static_cast<float>(p), static_cast<float>(1.0 / (1.0 - p)),
+                seed, offset);
+        });
+        check_launch("dropout");
+    });
+}
+
+int tp_b200_masked_scale(const tpb_tensor* dx, const tpb_tensor* dy, const tpb_tensor* mask, double scale,
+                         void* stream) {
+    return guarded([&] {
+        require_dense(dx, "masked_scale result");
+        require_dense(dy, "masked_scale grad");
+        require_dense(mask, "masked_scale mask");
+        TPB_CHECK(is_floating(dy->dtype) && dx->dtype == dy->dtype && mask->dtype == TPB_BOOL,
+                  "masked_scale: floating grad and result of one dtype, bool mask");
+        const int64_t n = numel_of(*dy);
+        TPB_CHECK(numel_of(*dx) == n && numel_of(*mask) == n, "masked_scale: sizes differ");
+        if (n == 0) return;
+        const int dev = device_of(dy->data);
+        DeviceGuard guard(dev);
+        cudaStream_t s = resolve_stream(stream, dev);
+        const unsigned grid = static_cast<unsigned>(
+            std::max<int64_t>(1, std::min<int64_t>(blocks_for(n, kThreads), int64_t(num_sms(dev)) * 16)));
+        TPB_DISPATCH_FLOAT(dy->dtype, "masked_scale", {
+            masked_scale_kernel<scalar_t><<<grid, kThreads, 0, s>>>(
+                static_cast<const scalar_t*>(dy->data), static_cast<const bool*>(mask->data),
+                static_cast<scalar_t*>(dx->data), n, scale);
+        });
+        check_launch("masked_scale");
     });
 }
 

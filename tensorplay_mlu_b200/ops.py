@@ -935,6 +935,81 @@ def nll_loss_backward(grad_output, self, target, weight, reduction: int, ignore_
     return dx
 
 
+def _dropout_seed() -> int:
+    """A 64-bit Philox key drawn from PyTorch's default host generator, so
+    torch.manual_seed reproduces the masks."""
+    return int(torch.randint(0, 2 ** 62, (1,)).item())
+
+
+def native_dropout(input, p: float, train=True):
+    """``native_dropout`` (NNKernels.cpp:164-196): (output, mask); kept
+    elements scaled by 1 / (1 - p)."""
+    _require_device(input)
+    if not input.dtype.is_floating_point:
+        raise RuntimeError(f"native_dropout: expected a floating input, got {input.dtype}")
+    if not 0.0 <= p <= 1.0:
+        raise RuntimeError(f"native_dropout: probability must be in [0, 1], got {p}")
+    if train is False or p == 0.0:
+        return clone(input), full_like(input, True, dtype=torch.bool)
+    if p == 1.0:
+        return zeros_like(input), full_like(input, False, dtype=torch.bool)
+    x = _dense(input)
+    out = _empty(input.shape, input.dtype, input.device)
+    mask = _empty(input.shape, torch.bool, input.device)
+    if x.numel():
+        N.check(_lib().tp_b200_dropout(describe(out), describe(mask), describe(x), float(p), _dropout_seed(), 0,
+                                       _stream(input)), "native_dropout")
+    return out, mask
+
+
+def native_dropout_backward(grad_output, mask, scale: float):
+    """``native_dropout_backward`` (NNKernels.cpp:222-236): grad * mask * scale."""
+    _require_device(grad_output, mask)
+    dx = _empty(grad_output.shape, grad_output.dtype, grad_output.device)
+    if dx.numel():
+        N.check(_lib().tp_b200_masked_scale(describe(dx), describe(_dense(grad_output)),
+                                            describe(_dense(_to_dtype(mask, torch.bool))), float(scale),
+                                            _stream(grad_output)), "native_dropout_backward")
+    return dx
+
+
+def embedding(weight, indices, padding_idx: int = -1, scale_grad_by_freq: bool = False, sparse: bool = False):
+    """``embedding`` (NNKernels.cpp:242-267): rows of ``weight`` at ``indices``
+    (index_select's row-vector copies)."""
+    _require_device(weight)
+    _index_tensor(indices, "embedding")
+    if weight.dim() != 2:
+        raise RuntimeError("embedding: weight must be 2-d")
+    rows = index_select(weight, 0, indices.reshape(-1))
+    return rows.reshape(list(indices.shape) + [weight.shape[1]])
+
+
+def embedding_dense_backward(grad_output, indices, num_weights: int, padding_idx: int = -1,
+                             scale_grad_by_freq: bool = False):
+    """``embedding_dense_backward`` (NNKernels.cpp:269-300): gradient rows
+    summed into their index (the padding row stays zero); with
+    scale_grad_by_freq each row divided by how often its index occurs."""
+    _require_device(grad_output)
+    _index_tensor(indices, "embedding_dense_backward")
+    dim = grad_output.shape[-1]
+    g = grad_output.reshape(-1, dim)
+    idx = indices.reshape(-1)
+    out = index_select_backward(g, [int(num_weights), int(dim)], 0, idx)
+    if scale_grad_by_freq:
+        ones = full_like(idx, 1, dtype=torch.float32).reshape(-1, 1)
+        counts = index_select_backward(ones, [int(num_weights), 1], 0, idx)
+        counts = where_self(gt_zero(counts), counts, full_like(counts, 1.0))
+        out = div_Tensor(out, _to_dtype(counts, out.dtype))
+    if 0 <= padding_idx < num_weights:
+        fill_(out[padding_idx], 0)
+    return out
+
+
+def gt_zero(t):
+    """t > 0 as bool, on the device (sign test through the unary kernels)."""
+    return _to_dtype(relu(t), torch.bool)
+
+
 def cross_entropy(input, target, weight=None, reduction: int = 1, ignore_index: int = -100):
     """cross_entropy over class dimension 1 of an (N, C) input, as TensorPlay
     composes it: nll_loss(log_softmax(input, 1), target)."""
@@ -943,6 +1018,194 @@ def cross_entropy(input, target, weight=None, reduction: int = 1, ignore_index: 
 
 def layer_norm(input, normalized_shape, weight=None, bias=None, eps: float = 1e-5):
     return native_layer_norm(input, normalized_shape, weight, bias, eps)[0]
+
+
+# -------------------------------------------------------------------- index
+
+_SCATTER_MODES = {None: 0, "": 0, "add": 1, "sum": 1, "multiply": 2, "prod": 2, "amax": 3, "amin": 4,
+                  "mean": 5}
+
+
+def _index_tensor(index, what):
+    _require_device(index)
+    if index.dtype not in (torch.int64, torch.int32):
+        raise RuntimeError(f"{what}: index must be int64 or int32, got {index.dtype}")
+    return index
+
+
+def _norm_dim(dim: int, nd: int, what: str) -> int:
+    n = max(nd, 1)
+    if not -n <= dim < n:
+        raise IndexError(f"{what}: dimension {dim} out of range for a {nd}-d tensor")
+    return dim % n
+
+
+def gather(self, dim: int, index, sparse_grad: bool = False):
+    """``gather`` (IndexKernels.cpp:45-69, 167-172): result shaped like index."""
+    _require_device(self)
+    _index_tensor(index, "gather")
+    d = _norm_dim(dim, self.dim(), "gather")
+    out = _empty(index.shape, self.dtype, self.device)
+    if out.numel():
+        N.check(_lib().tp_b200_gather(describe(out), describe(self), describe(index), d, _stream(self)),
+                "gather")
+    return out
+
+
+def _scatter_into(out, dim, index, src, mode: int, include_self: bool, what: str):
+    if index.numel():
+        N.check(_lib().tp_b200_scatter(describe(out), describe(index), describe(src), int(dim), int(mode),
+                                       int(include_self), _stream(out)), what)
+    return out
+
+
+def gather_backward(grad, self, dim: int, index, sparse_grad: bool = False):
+    """``gather_backward`` (IndexKernels.cpp:151-182): zeros of self's shape
+    accumulating grad at index."""
+    _require_device(grad)
+    _index_tensor(index, "gather_backward")
+    d = _norm_dim(dim, self.dim(), "gather_backward")
+    out = zeros_like(self, dtype=grad.dtype)
+    return _scatter_into(out, d, index, grad, 1, True, "gather_backward")
+
+
+def index_select(self, dim: int, index):
+    """``index_select`` (IndexKernels.cpp:184-209)."""
+    _require_device(self)
+    _index_tensor(index, "index_select")
+    if index.dim() > 1:
+        raise RuntimeError("index_select: index must be 0-d or 1-d")
+    d = _norm_dim(dim, self.dim(), "index_select")
+    x = _dense(self)
+    shape = list(self.shape)
+    if shape:
+        shape[d] = index.numel()
+    out = _empty(shape, self.dtype, self.device)
+    if out.numel():
+        N.check(_lib().tp_b200_index_select(describe(out), describe(x), describe(index), d, _stream(self)),
+                "index_select")
+    return out
+
+
+def index_select_backward(grad, self_sizes, dim: int, index):
+    """``index_select_backward`` (IndexKernels.cpp:211-219): zeros of
+    self_sizes with grad's slices added at index."""
+    _require_device(grad)
+    _index_tensor(index, "index_select_backward")
+    d = _norm_dim(dim, len(self_sizes), "index_select_backward")
+    out = torch.empty(tuple(int(x) for x in self_sizes), dtype=grad.dtype, device=grad.device)
+    fill_(out, 0)
+    g = _dense(grad)
+    if g.numel():
+        N.check(_lib().tp_b200_index_add(describe(out), describe(g), describe(index), d, _stream(grad)),
+                "index_select_backward")
+    return out
+
+
+def _scatter_common(self, dim, index, src, reduce, include_self, what):
+    _require_device(self, src)
+    _index_tensor(index, what)
+    if reduce not in _SCATTER_MODES:
+        raise RuntimeError(f"{what}: unknown reduction {reduce!r}")
+    dt = binary_result_dtype(self, src)
+    d = _norm_dim(dim, self.dim(), what)
+    out = clone(_to_dtype(self, dt))
+    if not out.is_contiguous():
+        out = contiguous(out)
+    return _scatter_into(out, d, index, _to_dtype(src, dt), _SCATTER_MODES[reduce], include_self, what)
+
+
+def _scatter_inplace(self, dim, index, src, reduce, what):
+    _require_device(self, src)
+    _index_tensor(index, what)
+    if reduce not in _SCATTER_MODES:
+        raise RuntimeError(f"{what}: unknown reduction {reduce!r}")
+    if binary_result_dtype(self, src) != self.dtype:
+        raise RuntimeError(f"{what}: result type {binary_result_dtype(self, src)} can't be cast to {self.dtype}")
+    d = _norm_dim(dim, self.dim(), what)
+    mode = _SCATTER_MODES[reduce]
+    target = self if (mode != 5 or self.is_contiguous()) else contiguous(self)
+    _scatter_into(target, d, index, _to_dtype(src, self.dtype), mode, True, what)
+    if target is not self:
+        copy_(self, target)
+    return self
+
+
+def scatter_add(self, dim: int, index, src):
+    """``scatter_add`` (IndexKernels.cpp:221-227)."""
+    return _scatter_common(self, dim, index, src, "add", True, "scatter_add")
+
+
+def scatter_add_(self, dim: int, index, src):
+    """``scatter_add_`` (IndexKernels.cpp:229-237)."""
+    return _scatter_inplace(self, dim, index, src, "add", "scatter_add_")
+
+
+def scatter_reduce_op(self, dim: int, index, src, reduce=None):
+    """``scatter.reduce`` (IndexKernels.cpp:239-249): replace when reduce is
+    None, else add / multiply / amax / amin / mean including self."""
+    return _scatter_common(self, dim, index, src, reduce, True, "scatter")
+
+
+def scatter_reduce_op_(self, dim: int, index, src, reduce=None):
+    """``scatter_.reduce`` (IndexKernels.cpp:251-264)."""
+    return _scatter_inplace(self, dim, index, src, reduce, "scatter_")
+
+
+def scatter_reduce(self, dim: int, index, src, reduce: str, include_self: bool = True):
+    """``scatter_reduce.two`` (IndexKernels.cpp:266-275): sum / prod / mean /
+    amax / amin, with or without self."""
+    if reduce not in ("sum", "prod", "mean", "amax", "amin"):
+        raise RuntimeError(f"scatter_reduce: reduce must be sum, prod, mean, amax or amin, got {reduce!r}")
+    return _scatter_common(self, dim, index, src, reduce, include_self, "scatter_reduce")
+
+
+def _scan(self, dim, dtype, product: bool, what: str):
+    _require_device(self)
+    out_dtype = dtype if dtype is not None else self.dtype
+    d = _norm_dim(dim, self.dim(), what)
+    x = _dense(_to_dtype(self, out_dtype))
+    out = _empty(self.shape, out_dtype, self.device)
+    if out.numel():
+        N.check(_lib().tp_b200_scan(int(product), describe(out), describe(x), d, _stream(self)), what)
+    return out
+
+
+def cumsum(self, dim: int, dtype=None):
+    """``cumsum`` (IndexKernels.cpp:277-283): result in ``dtype`` or self's dtype."""
+    return _scan(self, dim, dtype, False, "cumsum")
+
+
+def cumsum_(self, dim: int, dtype=None):
+    if dtype is not None and dtype != self.dtype:
+        raise RuntimeError("cumsum_: dtype must match the tensor")
+    return copy_(self, _scan(self, dim, None, False, "cumsum_"))
+
+
+def cumprod(self, dim: int, dtype=None):
+    """``cumprod`` (IndexKernels.cpp:295-301)."""
+    return _scan(self, dim, dtype, True, "cumprod")
+
+
+def cumprod_(self, dim: int, dtype=None):
+    if dtype is not None and dtype != self.dtype:
+        raise RuntimeError("cumprod_: dtype must match the tensor")
+    return copy_(self, _scan(self, dim, None, True, "cumprod_"))
+
+
+def where_self(condition, self, other):
+    """``where.self`` (IndexKernels.cpp:313-349): broadcast select, operands
+    promoted to their common dtype."""
+    _require_device(condition, self, other)
+    if condition.dtype != torch.bool:
+        raise RuntimeError(f"where: expected a bool condition, got {condition.dtype}")
+    dt = binary_result_dtype(self, other)
+    shape = torch.broadcast_shapes(condition.shape, self.shape, other.shape)
+    out = _empty(shape, dt, self.device)
+    if out.numel():
+        N.check(_lib().tp_b200_where(describe(out), describe(condition), describe(_to_dtype(self, dt)),
+                                     describe(_to_dtype(other, dt)), _stream(self)), "where")
+    return out
 
 
 # ---------------------------------------------------------------- registry
@@ -1023,4 +1286,23 @@ KERNELS = {
     "native_layer_norm_backward": native_layer_norm_backward,
     "nll_loss": nll_loss,
     "nll_loss_backward": nll_loss_backward,
+    # IndexKernels.cpp:352-367
+    "gather": gather,
+    "gather_backward": gather_backward,
+    "index_select": index_select,
+    "index_select_backward": index_select_backward,
+    "scatter_add": scatter_add,
+    "scatter_add_": scatter_add_,
+    "scatter.reduce": scatter_reduce_op,
+    "scatter_.reduce": scatter_reduce_op_,
+    "scatter_reduce.two": scatter_reduce,
+    "cumsum": cumsum,
+    "cumsum_": cumsum_,
+    "cumprod": cumprod,
+    "cumprod_": cumprod_,
+    "where.self": where_self,
+    "native_dropout": native_dropout,
+    "native_dropout_backward": native_dropout_backward,
+    "embedding": embedding,
+    "embedding_dense_backward": embedding_dense_backward,
 }

@@ -189,6 +189,37 @@ def main() -> None:
                 dx = aten.nll_loss_backward(g, x, t, w, red, -100, total)
                 add("nll_loss_backward", f"nll_loss_backward_{tag}", [g, x, t, total] + ([w] if w_on else []), dx,
                     reduction=red)
+    # ---- index family (IndexKernels.cpp:352-367): gather, index_select, scatter*, scans, where
+    g = torch.Generator().manual_seed(21)
+    for dt in float_types + [torch.int32, torch.int64]:
+        x = rand(5, 6, dtype=dt, seed=22, scale=3.0) if dt.is_floating_point else randint(5, 6, low=-50, high=50, dtype=dt, seed=22)
+        idx = torch.randint(0, 5, (4, 6), generator=g)
+        add("gather", f"gather_d0_{dt}", [x, idx], torch.gather(x, 0, idx), dim=0)
+        idx1 = torch.randint(-6, 6, (5, 3), generator=g)
+        add("gather", f"gather_d1_neg_{dt}", [x, idx1], torch.gather(x, 1, idx1 % 6), dim=1)
+        sel = torch.tensor([4, 0, 2, 2, -1])
+        add("index_select", f"index_select_{dt}", [x, sel], torch.index_select(x, 0, sel % 5), dim=0)
+        src = rand(4, 6, dtype=dt, seed=23) if dt.is_floating_point else randint(4, 6, low=-9, high=9, dtype=dt, seed=23)
+        add("scatter", f"scatter_add_{dt}", [x, idx, src], torch.scatter_add(x, 0, idx, src), dim=0, reduce="add",
+            include_self=True)
+        perm = torch.stack([torch.randperm(5, generator=g)[:4] for _ in range(6)], 1)  # no duplicates
+        add("scatter", f"scatter_replace_{dt}", [x, perm, src], torch.scatter(x, 0, perm, src), dim=0, reduce=None,
+            include_self=True)
+        for red in ("sum", "prod", "amax", "amin", "mean"):
+            for inc in (True, False):
+                want = x.scatter_reduce(0, idx, src, reduce=red, include_self=inc)
+                add("scatter", f"scatter_reduce_{red}_{'self' if inc else 'noself'}_{dt}", [x, idx, src], want,
+                    dim=0, reduce=red, include_self=inc)
+        add("scan", f"cumsum_d1_{dt}", [x], torch.cumsum(x, 1, dtype=dt), dim=1, product=False)
+        add("scan", f"cumsum_d0_{dt}", [x], torch.cumsum(x, 0, dtype=dt), dim=0, product=False)
+        xs = (x.double() / 4).to(dt) if dt.is_floating_point else (x % 3).to(dt)
+        add("scan", f"cumprod_d1_{dt}", [xs], torch.cumprod(xs, 1, dtype=dt), dim=1, product=True)
+        cond = torch.rand(5, 1, generator=g) > 0.5
+        other = src[:1]
+        add("where", f"where_{dt}", [cond, x, other], torch.where(cond, x, other))
+        gsrc = rand(5, 6, dtype=dt, seed=24) if dt.is_floating_point else randint(5, 6, low=-9, high=9, dtype=dt, seed=24)
+        add("index_add", f"index_select_backward_{dt}", [sel, gsrc], torch.zeros(5, 6, dtype=dt).index_add(0, sel % 5, gsrc),
+            shape=[5, 6], dim=0)
     # ---- casts (test_mlu.py:90-98) and round trips (:64-69): exact
     src = rand(3, 9, scale=4.0)
     for s, d in ((torch.float32, torch.float16), (torch.float16, torch.float32),

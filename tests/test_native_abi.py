@@ -106,9 +106,13 @@ def test_kernel_registry_matches_the_reference_registrations():
         "_softmax", "_log_softmax", "_softmax_backward_data", "_log_softmax_backward_data",
         "mm", "bmm", "addmm", "matmul", "linear",
     }
-    # NNKernels.cpp:399-410, the normalisation and loss part of that block
-    # (dropout and embedding are not registered yet).
-    expected |= {"native_layer_norm", "native_layer_norm_backward", "nll_loss", "nll_loss_backward"}
+    # NNKernels.cpp:399-410.
+    expected |= {"native_layer_norm", "native_layer_norm_backward", "nll_loss", "nll_loss_backward",
+                 "native_dropout", "native_dropout_backward", "embedding", "embedding_dense_backward"}
+    # IndexKernels.cpp:352-367.
+    expected |= {"gather", "gather_backward", "index_select", "index_select_backward", "scatter_add",
+                 "scatter_add_", "scatter.reduce", "scatter_.reduce", "scatter_reduce.two", "cumsum", "cumsum_",
+                 "cumprod", "cumprod_", "where.self"}
     assert set(tpb.ops.KERNELS) == expected
 
 

@@ -134,3 +134,44 @@ def test_cross_entropy_training_step_matches_host(ops):
     for got, p in zip((g_w1, g_b1, g_w2, g_b2), model.parameters()):
         assert (ops.to_host(got) - p.grad).abs().max().item() < 1e-4
     assert abs(ops.item(ops.cross_entropy(logits, dt)) - loss_ref.item()) < 1e-4
+
+
+@pytest.mark.parametrize("dtype", FLOATS)
+def test_dropout_matches_the_oracle_generator(ops, dtype):
+    x = rand(333, 257, dtype=dtype, seed=9)
+    torch.manual_seed(123)
+    out, mask = ops.native_dropout(ops.to_device(x), 0.3, True)
+    torch.manual_seed(123)
+    seed = int(torch.randint(0, 2 ** 62, (1,)).item())
+    want_out, want_mask = O.dropout(x, 0.3, seed)
+    assert torch.equal(ops.to_host(mask), want_mask)
+    assert torch.equal(ops.to_host(out), want_out)
+    kept = want_mask.float().mean().item()
+    assert abs(kept - 0.7) < 0.01
+    dy = rand(333, 257, dtype=dtype, seed=10)
+    dx = ops.native_dropout_backward(ops.to_device(dy), mask, 1 / 0.7)
+    want_dx = torch.where(want_mask, (dy.double() / 0.7), torch.zeros((), dtype=torch.float64)).to(dtype)
+    assert_close(dx, want_dx, dtype)
+    # Evaluation and the edge probabilities need no generator.
+    same, m = ops.native_dropout(ops.to_device(x), 0.5, False)
+    assert torch.equal(ops.to_host(same), x) and bool(ops.to_host(m).all())
+    zero, m = ops.native_dropout(ops.to_device(x), 1.0, True)
+    assert not bool(ops.to_host(zero).any()) and not bool(ops.to_host(m).any())
+
+
+def test_embedding_forward_backward(ops):
+    weight = rand(1000, 64, seed=11)
+    g = torch.Generator().manual_seed(12)
+    idx = torch.randint(0, 1000, (7, 9), generator=g)
+    idx[0, :3] = 3  # duplicates and the padding index
+    out = ops.embedding(ops.to_device(weight), ops.to_device(idx), 3)
+    assert_close(out, O.index_select(weight, 0, idx.reshape(-1)).reshape(7, 9, 64), torch.float32)
+    grad = rand(7, 9, 64, seed=13)
+    for freq in (False, True):
+        got = ops.embedding_dense_backward(ops.to_device(grad), ops.to_device(idx), 1000, 3, freq)
+        want = O.index_add_zeros([1000, 64], 0, idx.reshape(-1), grad.reshape(-1, 64))
+        if freq:
+            counts = torch.bincount(idx.reshape(-1), minlength=1000).clamp(min=1).to(torch.float32)
+            want = want / counts[:, None]
+        want[3] = 0
+        assert_close(got, want, torch.float32, scale=4)

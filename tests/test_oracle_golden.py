@@ -58,6 +58,18 @@ def oracle_output(case):
         return O.gemm(ins[0], ins[1])
     if kind == "cast":
         return O.cast(ins[0], p["dtype"])
+    if kind == "gather":
+        return O.gather(ins[0], p["dim"], ins[1])
+    if kind == "index_select":
+        return O.index_select(ins[0], p["dim"], ins[1])
+    if kind == "scatter":
+        return O.scatter(ins[0], p["dim"], ins[1], ins[2], p["reduce"], p["include_self"])
+    if kind == "scan":
+        return O.scan(ins[0], p["dim"], p["product"])
+    if kind == "where":
+        return O.where(*ins)
+    if kind == "index_add":
+        return O.index_add_zeros(p["shape"], p["dim"], ins[0], ins[1])
     if kind == "layer_norm":
         x, w, b = (ins + [None, None])[:3]
         y, mean, rstd = O.layer_norm(x, p["norm"], w, b, p["eps"])
@@ -79,7 +91,7 @@ def oracle_output(case):
     raise AssertionError(kind)
 
 
-EXACT_KINDS = {"cast", "scalar_chain"}
+EXACT_KINDS = {"cast", "scalar_chain", "gather", "index_select", "where"}
 
 
 @pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
@@ -106,7 +118,7 @@ def test_golden_covers_every_family():
     kinds = {c["kind"] for c in CASES}
     assert {"binary", "scalar", "unary", "unary_backward", "reduce", "softmax", "softmax_backward",
             "gemm", "cast", "scalar_chain", "layer_norm", "layer_norm_backward", "nll_loss",
-            "nll_loss_backward"} <= kinds
+            "nll_loss_backward", "gather", "index_select", "scatter", "scan", "where", "index_add"} <= kinds
 
 
 def test_oracle_mlp_step_matches_torch_autograd():
@@ -133,3 +145,14 @@ def test_oracle_mlp_step_matches_torch_autograd():
     assert abs(got_loss - loss.item()) <= 2e-2 * max(1.0, loss.item())
     for got, ref in zip(ow, want):
         assert (got.float() - ref).abs().max().item() <= 2e-2 * max(ref.abs().max().item(), 1.0)
+
+
+def test_philox_matches_the_published_known_answers():
+    """Philox-4x32-10 (the dropout generator) against the Random123
+    known-answer vectors for 10 rounds."""
+    kat = [((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+           ((0xFFFFFFFF,) * 4, (0xFFFFFFFF, 0xFFFFFFFF), (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+           ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+            (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1))]
+    for ctr, key, want in kat:
+        assert tuple(O.philox4x32_10(ctr, key)) == want
