@@ -377,6 +377,18 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     pg = D.create(_PrefixStore("nccl_b200", host.store), rank, world, device=local, timeout_s=300) \
         if world > 1 else None
 
+    # Kernel-level extras (op sweep, GEMM set) at N = 1: measured before the
+    # training loop by default, so their kernels run at the clocks a kernel
+    # gets on its own rather than just after seconds at the power cap.
+    pre = {}
+    if world == 1 and not args.no_extras and args.extras_order == "first":
+        with ClockSampler(local) as extra_clocks:
+            pre["op_sweep"] = op_sweep(ops, hbm_peak)
+            pre["gemm_set"] = gemm_set(ops, bf16_peak)
+        pre["extras_clocks"] = extra_clocks.summary()
+        torch.cuda.empty_cache()
+        tpb.runtime.empty_cache()
+
     # TPB200_DW1_SLICES overrides how many slices the last gradient bucket is
     # exchanged in (A/B measurements; the default is MLPConfig's).
     slices = int(os.environ.get("TPB200_DW1_SLICES", MLPConfig.dw1_slices))
@@ -504,8 +516,13 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         del model
         torch.cuda.empty_cache()
         tpb.runtime.empty_cache()
-        line["op_sweep"] = op_sweep(ops, hbm_peak)
-        line["gemm_set"] = gemm_set(ops, bf16_peak)
+        if pre:
+            line.update(pre)
+        else:
+            with ClockSampler(local) as extra_clocks:
+                line["op_sweep"] = op_sweep(ops, hbm_peak)
+                line["gemm_set"] = gemm_set(ops, bf16_peak)
+            line["extras_clocks"] = extra_clocks.summary()
         cpu_value, threads, _ = cpu_mlp_throughput(2, 1, 16)
         line["cpu_baseline"] = {"value": round(cpu_value, 2), "unit": UNIT, "cores": threads, "kind": "port",
                                 "sample": "16 rows per step of the 8192-row batch, full 134M-parameter weights, "
@@ -592,6 +609,8 @@ def main() -> None:
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-extras", action="store_true", help="skip the op sweep, GEMM set and CPU baseline")
+    p.add_argument("--extras-order", choices=["first", "last"], default="first",
+                   help="run the op sweep and GEMM set before (default) or after the training loop")
     p.add_argument("--only", default=None,
                    help="run one kernel workload --steps times and exit (for ncu captures)")
     p.add_argument("--sweep-only", action="store_true",
