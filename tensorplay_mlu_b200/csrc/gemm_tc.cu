@@ -3,7 +3,7 @@
 // persistent, warp-specialised CTA per SM (tensorplay-mlu runs these
 // products on cnnlMatMul_v2 / cnnlStrideBatchMatMul_v3, BlasKernels.cpp:202-242).
 //
-// CTA layout (192 threads, one CTA per SM):
+// CTA layout (320 threads, one CTA per SM):
 //   warp 0      TMA producer: one elected thread fills a ring of kStages
 //               shared-memory stages (A: 128 x 64 bf16, B: BN x 64 bf16) and
 //               arms each stage's "full" mbarrier with the byte count;
@@ -12,9 +12,12 @@
 //               stage and releases the stage with tcgen05.commit on its
 //               "empty" mbarrier; after a tile's last stage it commits to the
 //               accumulator's "full" barrier;
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time from the lane
-//               quadrant the warp may access, apply alpha/beta/addend,
-//               convert and store; then release the accumulator.
+//   warps 2..9  epilogue: two warps per TMEM lane quadrant (the lanes a
+//               warp may access), each taking half of the columns:
+//               tcgen05.ld 32 columns at a time (the next chunk's load
+//               issued before the current one is stored), apply
+//               alpha/beta/addend, convert and store; then release the
+//               accumulator.
 // Two accumulators let the epilogue of tile i overlap the mainloop of
 // tile i+1.  Tiles are visited in groups of kGroupM row-tiles so the CTAs in
 // flight share A and B panels in L2.
@@ -52,7 +55,8 @@ void copy_impl(const tpb_tensor& dst, const tpb_tensor& src, cudaStream_t stream
 
 namespace {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // warp 0 producer, warp 1 MMA, warps 2-9 epilogue
+constexpr int kEpilogueWarps = 8;
 constexpr int kBM = 128;
 constexpr int kGroupM = 16;
 
@@ -166,6 +170,7 @@ struct TcParams {
     int64_t sci_b, sci_m, sci_n;
     float alpha, beta;
     int vec_store;    // 16-byte stores allowed
+    int tma_store;    // result written through the C tensor map (TMA stores)
     int* err;
 };
 
@@ -225,9 +230,16 @@ __device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap* ma
     }
 }
 
+// Per epilogue warp: one 32 x 32 tile of the result type, staged for a TMA
+// store (64-byte-swizzled rows for 16-bit types, 128-byte for fp32).
+template <typename T>
+__host__ __device__ constexpr size_t staging_bytes() {
+    return size_t(32) * 32 * sizeof(T);
+}
+
 template <typename T, int BN>
 constexpr size_t tc_smem_bytes() {
-    return size_t(TcShape<BN>::kStages) * (kBM * 128 + BN * 128) + 1024 + 256;
+    return size_t(TcShape<BN>::kStages) * (kBM * 128 + BN * 128) + kEpilogueWarps * staging_bytes<T>() + 1024 + 256;
 }
 
 __device__ __forceinline__ void tile_coords(const TcParams& p, int tile, int& b, int& mt, int& nt) {
@@ -243,9 +255,114 @@ __device__ __forceinline__ void tile_coords(const TcParams& p, int tile, int& b,
     nt = q / gsize;
 }
 
+// The epilogue of one accumulator: this warp's 32 rows (its TMEM lane
+// quadrant, t_rows = TMEM address of row 0 / column 0 of the accumulator)
+// for columns [col0, col0 + NCOL).  The load of chunk c + 1 is issued before
+// chunk c is converted and stored, so TMEM reads overlap the global stores.
+template <typename T, int NCOL>
+__device__ __forceinline__ void store_accumulator(const TcParams& p, uint32_t t_rows, int col0, int b, int64_t gm,
+                                                  int64_t n_tile0, bool row_ok) {
+    constexpr int kChunks = NCOL / 32;
+    T* crow = static_cast<T*>(p.c) + b * p.sc_b + gm * p.sc_m;
+    const T* cin = static_cast<const T*>(p.cin);
+    uint32_t r[2][32];
+    __syncwarp();
+    tmem_ld32(t_rows + col0, r[0]);
+#pragma unroll
+    for (int chunk = 0; chunk < kChunks; ++chunk) {
+        tmem_wait_ld();
+        if (chunk + 1 < kChunks) tmem_ld32(t_rows + col0 + (chunk + 1) * 32, r[(chunk + 1) & 1]);
+        const uint32_t* rc = r[chunk & 1];
+        const int64_t n_base = n_tile0 + col0 + chunk * 32;
+        if (row_ok && n_base < p.N) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(rc[j]);
+            if (cin != nullptr) {
+                const T* crow_in = cin + b * p.sci_b + gm * p.sci_m;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (n_base + j < p.N) v[j] += p.beta * load_as<float>(crow_in[(n_base + j) * p.sci_n]);
+                }
+            }
+            if (p.vec_store && n_base + 32 <= p.N) {
+                constexpr int V = 16 / sizeof(T);
+#pragma unroll
+                for (int j = 0; j < 32; j += V) {
+                    Vec<T, V> o;
+#pragma unroll
+                    for (int q = 0; q < V; ++q) o.v[q] = store_as<T>(v[j + q]);
+                    *reinterpret_cast<Vec<T, V>*>(crow + n_base + j) = o;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (n_base + j < p.N) crow[n_base + j] = store_as<T>(v[j]);
+                }
+            }
+        }
+    }
+}
+
+// The same through shared memory and a TMA store: each chunk of 32 rows x
+// 32 columns is converted into this warp's staging tile (rows swizzled the
+// way the C tensor map expects, so the 32 lanes' 16-byte writes hit distinct
+// banks), then one lane stores the whole tile asynchronously in full lines.
+// TMA clips the tile at M and N.  row0: the warp's first row in C.
+template <typename T, int NCOL, bool BATCHED>
+__device__ __forceinline__ void store_accumulator_tma(const TcParams& p, const CUtensorMap* tmC, uint8_t* stage,
+                                                      uint32_t t_rows, int col0, int b, int64_t gm, int64_t row0,
+                                                      int64_t n_tile0, bool row_ok) {
+    constexpr int kChunks = NCOL / 32;
+    constexpr int kRowBytes = 32 * int(sizeof(T));  // 64 (16-bit) or 128 (fp32)
+    constexpr int kVecs = kRowBytes / 16;
+    const int lane = threadIdx.x & 31;
+    const T* cin = static_cast<const T*>(p.cin);
+    uint32_t r[2][32];
+    __syncwarp();
+    tmem_ld32(t_rows + col0, r[0]);
+#pragma unroll
+    for (int chunk = 0; chunk < kChunks; ++chunk) {
+        tmem_wait_ld();
+        if (chunk + 1 < kChunks) tmem_ld32(t_rows + col0 + (chunk + 1) * 32, r[(chunk + 1) & 1]);
+        const uint32_t* rc = r[chunk & 1];
+        const int64_t n_base = n_tile0 + col0 + chunk * 32;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(rc[j]);
+        if (cin != nullptr && row_ok) {
+            const T* crow_in = cin + b * p.sci_b + gm * p.sci_m;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                if (n_base + j < p.N) v[j] += p.beta * load_as<float>(crow_in[(n_base + j) * p.sci_n]);
+            }
+        }
+        Vec<T, 32> packed;
+        pack_vec(v, packed);
+        // The previous store from this staging tile has finished reading it.
+        if (lane == 0) bulk_wait_group_read0();
+        __syncwarp();
+        const uint4* src = reinterpret_cast<const uint4*>(&packed);
+        uint8_t* row = stage + lane * kRowBytes;
+#pragma unroll
+        for (int q = 0; q < kVecs; ++q) {
+            const int phys = kRowBytes == 64 ? (q ^ ((lane >> 1) & 3)) : (q ^ (lane & 7));
+            *reinterpret_cast<uint4*>(row + phys * 16) = src[q];
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && n_base < p.N && row0 < p.M) {
+            if constexpr (BATCHED) tma_store_3d(tmC, smem_addr(stage), int(n_base), int(row0), b);
+            else tma_store_2d(tmC, smem_addr(stage), int(n_base), int(row0));
+            bulk_commit_group();
+        }
+    }
+}
+
 template <typename T, int BN, bool A_MN, bool B_MN, bool BATCHED>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC,
                    const TcParams p) {
     using E = TcElem<T>;
     constexpr int kStages = TcShape<BN>::kStages;
@@ -261,7 +378,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* smem_a = smem;
     uint8_t* smem_b = smem + kStages * kABytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_b + kStages * kBBytes);
+    uint8_t* staging = smem_b + kStages * kBBytes;  // kEpilogueWarps tiles for TMA stores
+    uint64_t* bars = reinterpret_cast<uint64_t*>(staging + kEpilogueWarps * staging_bytes<T>());
     uint64_t* full = bars;
     uint64_t* empty = bars + kStages;
     uint64_t* acc_full = bars + 2 * kStages;
@@ -280,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(smem_addr(&acc_full[a]), 1);
-            mbar_init(smem_addr(&acc_empty[a]), 4);
+            mbar_init(smem_addr(&acc_empty[a]), kEpilogueWarps);
         }
         mbar_init(smem_addr(drain), 1);
         *abort_flag = 0;
@@ -391,11 +509,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // --------------------------------------------------- epilogue --
-        const int quad = warp & 3;              // TMEM lane quadrant this warp may access
+        // Warps 2-9: lane quadrant warp & 3 (the TMEM lanes a warp may read),
+        // column half (warp - 2) / 4.
+        const int quad = warp & 3;
+        const int half = (warp - 2) / 4;
         const int row_in_tile = quad * 32 + lane;
         int local = 0;
-        T* c = static_cast<T*>(p.c);
-        const T* cin = static_cast<const T*>(p.cin);
         for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
             const int acc = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
@@ -407,48 +526,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             int b, mt, nt;
             tile_coords(p, tile, b, mt, nt);
             const int64_t gm = int64_t(mt) * kBM + row_in_tile;
-            const bool row_ok = gm < p.M;
-            T* crow = c + b * p.sc_b + gm * p.sc_m;
-            const uint32_t t_base = tmem_base + (uint32_t(quad * 32) << 16) + acc * BN;
-#pragma unroll 1
-            for (int chunk = 0; chunk < BN / 32; ++chunk) {
-                uint32_t r[32];
-                __syncwarp();
-                tmem_ld32(t_base + chunk * 32, r);
-                tmem_wait_ld();
-                const int64_t n_base = int64_t(nt) * BN + chunk * 32;
-                if (row_ok && n_base < p.N) {
-                    float v[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
-                    if (cin != nullptr) {
-                        const T* crow_in = cin + b * p.sci_b + gm * p.sci_m;
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            if (n_base + j < p.N) v[j] += p.beta * load_as<float>(crow_in[(n_base + j) * p.sci_n]);
-                        }
-                    }
-                    if (p.vec_store && n_base + 32 <= p.N) {
-                        constexpr int V = 16 / sizeof(T);
-#pragma unroll
-                        for (int j = 0; j < 32; j += V) {
-                            Vec<T, V> o;
-#pragma unroll
-                            for (int q = 0; q < V; ++q) o.v[q] = store_as<T>(v[j + q]);
-                            *reinterpret_cast<Vec<T, V>*>(crow + n_base + j) = o;
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            if (n_base + j < p.N) crow[n_base + j] = store_as<T>(v[j]);
-                        }
-                    }
-                }
+            const uint32_t t_rows = tmem_base + (uint32_t(quad * 32) << 16) + acc * BN;
+            if (p.tma_store) {
+                store_accumulator_tma<T, BN / 2, BATCHED>(p, &tmC, staging + (warp - 2) * staging_bytes<T>(), t_rows,
+                                                          half * (BN / 2), b, gm, gm - lane, int64_t(nt) * BN,
+                                                          gm < p.M);
+            } else {
+                store_accumulator<T, BN / 2>(p, t_rows, half * (BN / 2), b, gm, int64_t(nt) * BN, gm < p.M);
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_addr(&acc_empty[acc]));
+            if (lane == 0) mbar_arrive_relaxed(smem_addr(&acc_empty[acc]));
         }
+        // The TMA stores this warp issued are complete before the CTA leaves.
+        if (lane == 0) bulk_wait_group0();
     }
 
     tc_fence_before();
@@ -473,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 //     total bytes.
 //   * The leader's commits are multicast to the same barrier in both CTAs:
 //     "empty" (the stage may be refilled in both) and "acc_full".
-//   * Both CTAs' epilogue warps arrive on the leader's "acc_empty" (count 8).
+//   * Both CTAs' epilogue warps arrive on the leader's "acc_empty" (count 16).
 // Waits are bounded as in the 1-SM kernel; teardown is a cluster barrier
 // followed by the paired TMEM release.
 
@@ -497,6 +588,7 @@ __device__ __forceinline__ void cluster_sync() {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+
 
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
@@ -545,7 +637,7 @@ constexpr int kPairBN = 256;  // columns per CTA pair (each CTA stages 128 of B)
 
 template <typename T>
 constexpr size_t tc2_smem_bytes() {
-    return size_t(kPairStages) * (128 * 128 + 128 * 128) + 1024 + 256;
+    return size_t(kPairStages) * (128 * 128 + 128 * 128) + kEpilogueWarps * staging_bytes<T>() + 1024 + 256;
 }
 
 __device__ __forceinline__ void tile_coords_pair(const TcParams& p, int tile, int& b, int& mt, int& nt,
@@ -565,6 +657,7 @@ __device__ __forceinline__ void tile_coords_pair(const TcParams& p, int tile, in
 template <typename T, bool A_MN, bool B_MN, bool BATCHED>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmC,
                     const TcParams p, const int group_m) {
     using E = TcElem<T>;
     constexpr int kStages = kPairStages;
@@ -580,7 +673,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* smem_a = smem;
     uint8_t* smem_b = smem + kStages * kABytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_b + kStages * kBBytes);
+    uint8_t* staging = smem_b + kStages * kBBytes;  // kEpilogueWarps tiles for TMA stores
+    uint64_t* bars = reinterpret_cast<uint64_t*>(staging + kEpilogueWarps * staging_bytes<T>());
     uint64_t* full = bars;
     uint64_t* empty = bars + kStages;
     uint64_t* acc_full = bars + 2 * kStages;
@@ -603,7 +697,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(smem_addr(&acc_full[a]), 1);
-            mbar_init(smem_addr(&acc_empty[a]), 8);
+            mbar_init(smem_addr(&acc_empty[a]), 2 * kEpilogueWarps);
         }
         mbar_init(smem_addr(drain), 1);
         *abort_flag = 0;
@@ -707,10 +801,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else {
         // ------------------------------------------ epilogue (both CTAs) --
         const int quad = warp & 3;
+        const int half = (warp - 2) / 4;
         const int row_in_tile = int(rank) * 128 + quad * 32 + lane;
         int local = 0;
-        T* c = static_cast<T*>(p.c);
-        const T* cin = static_cast<const T*>(p.cin);
         const uint32_t leader_empty0 = map_to_cta(smem_addr(&acc_empty[0]), 0);
         const uint32_t leader_empty1 = map_to_cta(smem_addr(&acc_empty[1]), 0);
         for (int tile = cluster_id; tile < p.num_tiles; tile += num_clusters, ++local) {
@@ -724,48 +817,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             int b, mt, nt;
             tile_coords_pair(p, tile, b, mt, nt, group_m);
             const int64_t gm = int64_t(mt) * kPairBM + row_in_tile;
-            const bool row_ok = gm < p.M;
-            T* crow = c + b * p.sc_b + gm * p.sc_m;
-            const uint32_t t_base = tmem_base + (uint32_t(quad * 32) << 16) + acc * kPairBN;
-#pragma unroll 1
-            for (int chunk = 0; chunk < kPairBN / 32; ++chunk) {
-                uint32_t r[32];
-                __syncwarp();
-                tmem_ld32(t_base + chunk * 32, r);
-                tmem_wait_ld();
-                const int64_t n_base = int64_t(nt) * kPairBN + chunk * 32;
-                if (row_ok && n_base < p.N) {
-                    float v[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
-                    if (cin != nullptr) {
-                        const T* crow_in = cin + b * p.sci_b + gm * p.sci_m;
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            if (n_base + j < p.N) v[j] += p.beta * load_as<float>(crow_in[(n_base + j) * p.sci_n]);
-                        }
-                    }
-                    if (p.vec_store && n_base + 32 <= p.N) {
-                        constexpr int V = 16 / sizeof(T);
-#pragma unroll
-                        for (int j = 0; j < 32; j += V) {
-                            Vec<T, V> o;
-#pragma unroll
-                            for (int q = 0; q < V; ++q) o.v[q] = store_as<T>(v[j + q]);
-                            *reinterpret_cast<Vec<T, V>*>(crow + n_base + j) = o;
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            if (n_base + j < p.N) crow[n_base + j] = store_as<T>(v[j]);
-                        }
-                    }
-                }
+            const uint32_t t_rows = tmem_base + (uint32_t(quad * 32) << 16) + acc * kPairBN;
+            if (p.tma_store) {
+                store_accumulator_tma<T, kPairBN / 2, BATCHED>(p, &tmC, staging + (warp - 2) * staging_bytes<T>(),
+                                                               t_rows, half * (kPairBN / 2), b, gm, gm - lane,
+                                                               int64_t(nt) * kPairBN, gm < p.M);
+            } else {
+                store_accumulator<T, kPairBN / 2>(p, t_rows, half * (kPairBN / 2), b, gm, int64_t(nt) * kPairBN,
+                                                  gm < p.M);
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(acc == 0 ? leader_empty0 : leader_empty1);
+            if (lane == 0) mbar_arrive_cluster_relaxed(acc == 0 ? leader_empty0 : leader_empty1);
         }
+        if (lane == 0) bulk_wait_group0();
     }
 
     // Teardown: every thread of both CTAs reaches this point (no early
@@ -815,6 +880,23 @@ CUtensorMap make_map(const void* base, CUtensorMapDataType type, int es, int64_t
     return map;
 }
 
+// The result's tensor map for the TMA-store epilogue: boxes of 32 x 32
+// elements, 64-byte-swizzled rows for 16-bit types, 128-byte for fp32.
+CUtensorMap make_c_map(void* base, CUtensorMapDataType type, int es, int64_t N, int64_t M, int64_t row_stride,
+                       int64_t batch, int64_t batch_stride) {
+    CUtensorMap map;
+    const int rank = batch > 1 ? 3 : 2;
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(batch)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_stride * es), static_cast<cuuint64_t>(batch_stride * es)};
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = encode_fn()(&map, type, rank, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                   es == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    TPB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (result) failed (%d)", static_cast<int>(r));
+    return map;
+}
+
 bool tma_ok(const void* p, int es, int64_t other_stride, int64_t batch, int64_t batch_stride) {
     if (!aligned16(p)) return false;
     if (other_stride <= 0 || (other_stride * es) % 16 != 0) return false;
@@ -848,8 +930,8 @@ int choose_bn(int64_t M, int64_t N, int64_t batch, int sms) {
 }
 
 template <typename T, int BN, bool A_MN, bool B_MN, bool BATCHED>
-void launch_tc(const GemmProblem& p, const CUtensorMap& ma, const CUtensorMap& mb, TcParams& tp,
-               int dev, cudaStream_t stream) {
+void launch_tc(const GemmProblem& p, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+               TcParams& tp, int dev, cudaStream_t stream) {
     constexpr size_t smem = tc_smem_bytes<T, BN>();
     auto kern = gemm_tc_kernel<T, BN, A_MN, B_MN, BATCHED>;
     static bool configured[64] = {};
@@ -867,12 +949,13 @@ void launch_tc(const GemmProblem& p, const CUtensorMap& ma, const CUtensorMap& m
     tp.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (uint32_t(tp.a_mn) << 15) |
                (uint32_t(tp.b_mn) << 16) | (uint32_t(BN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
     const int grid = std::min(tp.num_tiles, num_sms(dev));
-    kern<<<grid, kThreads, smem, stream>>>(ma, mb, tp);
+    kern<<<grid, kThreads, smem, stream>>>(ma, mb, mc, tp);
     check_launch("gemm_tc");
 }
 
 template <typename T, bool A_MN, bool B_MN, bool BATCHED>
-void launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, TcParams& tp, int dev, cudaStream_t stream) {
+void launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, TcParams& tp, int dev,
+                cudaStream_t stream) {
     constexpr size_t smem = tc2_smem_bytes<T>();
     auto kern = gemm_tc2_kernel<T, A_MN, B_MN, BATCHED>;
     static bool configured[64] = {};
@@ -893,7 +976,7 @@ void launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, TcParams& tp, int 
     int group_m = static_cast<int>(std::max<int64_t>(1, (int64_t(32) << 20) / std::max<int64_t>(panel, 1)));
     group_m = std::min(group_m, tp.m_tiles);
     const int clusters = std::min(tp.num_tiles, num_sms(dev) / 2);
-    kern<<<2 * clusters, kThreads, smem, stream>>>(ma, mb, tp, group_m);
+    kern<<<2 * clusters, kThreads, smem, stream>>>(ma, mb, mc, tp, group_m);
     check_launch("gemm_tc2");
 }
 
@@ -901,31 +984,31 @@ void launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, TcParams& tp, int 
 // operands always arrive K-major, so only that instance is built for them.
 template <typename T, bool A_MN, bool B_MN, bool BATCHED>
 void launch_layout(bool pair, int bn, const GemmProblem& p, const CUtensorMap& ma, const CUtensorMap& mb,
-                   TcParams& tp, int dev, cudaStream_t stream) {
-    if (pair) launch_tc2<T, A_MN, B_MN, BATCHED>(ma, mb, tp, dev, stream);
-    else if (bn == 256) launch_tc<T, 256, A_MN, B_MN, BATCHED>(p, ma, mb, tp, dev, stream);
-    else launch_tc<T, 128, A_MN, B_MN, BATCHED>(p, ma, mb, tp, dev, stream);
+                   const CUtensorMap& mc, TcParams& tp, int dev, cudaStream_t stream) {
+    if (pair) launch_tc2<T, A_MN, B_MN, BATCHED>(ma, mb, mc, tp, dev, stream);
+    else if (bn == 256) launch_tc<T, 256, A_MN, B_MN, BATCHED>(p, ma, mb, mc, tp, dev, stream);
+    else launch_tc<T, 128, A_MN, B_MN, BATCHED>(p, ma, mb, mc, tp, dev, stream);
 }
 
 template <typename T>
 void launch_any(bool pair, int bn, const GemmProblem& p, const CUtensorMap& ma, const CUtensorMap& mb,
-                TcParams& tp, int dev, cudaStream_t stream) {
+                const CUtensorMap& mc, TcParams& tp, int dev, cudaStream_t stream) {
     const bool bt = tp.batched != 0;
     if constexpr (std::is_same<T, float>::value) {
         TPB_CHECK(!tp.a_mn && !tp.b_mn, "gemm: TF32 operands must be K-major");
-        if (bt) launch_layout<T, false, false, true>(pair, bn, p, ma, mb, tp, dev, stream);
-        else launch_layout<T, false, false, false>(pair, bn, p, ma, mb, tp, dev, stream);
+        if (bt) launch_layout<T, false, false, true>(pair, bn, p, ma, mb, mc, tp, dev, stream);
+        else launch_layout<T, false, false, false>(pair, bn, p, ma, mb, mc, tp, dev, stream);
     } else {
         const int code = (tp.a_mn ? 4 : 0) | (tp.b_mn ? 2 : 0) | (bt ? 1 : 0);
         switch (code) {
-            case 0: launch_layout<T, false, false, false>(pair, bn, p, ma, mb, tp, dev, stream); break;
-            case 1: launch_layout<T, false, false, true>(pair, bn, p, ma, mb, tp, dev, stream); break;
-            case 2: launch_layout<T, false, true, false>(pair, bn, p, ma, mb, tp, dev, stream); break;
-            case 3: launch_layout<T, false, true, true>(pair, bn, p, ma, mb, tp, dev, stream); break;
-            case 4: launch_layout<T, true, false, false>(pair, bn, p, ma, mb, tp, dev, stream); break;
-            case 5: launch_layout<T, true, false, true>(pair, bn, p, ma, mb, tp, dev, stream); break;
-            case 6: launch_layout<T, true, true, false>(pair, bn, p, ma, mb, tp, dev, stream); break;
-            default: launch_layout<T, true, true, true>(pair, bn, p, ma, mb, tp, dev, stream); break;
+            case 0: launch_layout<T, false, false, false>(pair, bn, p, ma, mb, mc, tp, dev, stream); break;
+            case 1: launch_layout<T, false, false, true>(pair, bn, p, ma, mb, mc, tp, dev, stream); break;
+            case 2: launch_layout<T, false, true, false>(pair, bn, p, ma, mb, mc, tp, dev, stream); break;
+            case 3: launch_layout<T, false, true, true>(pair, bn, p, ma, mb, mc, tp, dev, stream); break;
+            case 4: launch_layout<T, true, false, false>(pair, bn, p, ma, mb, mc, tp, dev, stream); break;
+            case 5: launch_layout<T, true, false, true>(pair, bn, p, ma, mb, mc, tp, dev, stream); break;
+            case 6: launch_layout<T, true, true, false>(pair, bn, p, ma, mb, mc, tp, dev, stream); break;
+            default: launch_layout<T, true, true, true>(pair, bn, p, ma, mb, mc, tp, dev, stream); break;
         }
     }
 }
@@ -1035,7 +1118,14 @@ bool gemm_tc_typed(const GemmProblem& p_in, int dev, cudaStream_t stream, CUtens
     tp.beta = static_cast<float>(p.beta);
     tp.vec_store = aligned16(p.c) && (p.sc_m * es) % 16 == 0 && (p.batch == 1 || (p.sc_b * es) % 16 == 0);
     tp.err = device_error_word(dev);
-    launch_any<T>(pair, bn, p, ma, mb, tp, dev, stream);
+    // The result through a C tensor map (TMA stores) when its layout allows.
+    // TPB200_NO_TMA_STORE=1 keeps the direct-store epilogue (A/B measurements).
+    static const bool no_tma_store = std::getenv("TPB200_NO_TMA_STORE") != nullptr;
+    const bool c_tma = !no_tma_store && aligned16(p.c) && p.sc_m > 0 && (p.sc_m * es) % 16 == 0 &&
+                       (p.batch == 1 || (p.sc_b > 0 && (p.sc_b * es) % 16 == 0));
+    tp.tma_store = c_tma ? 1 : 0;
+    const CUtensorMap mc = c_tma ? make_c_map(p.c, type, es, p.N, p.M, p.sc_m, p.batch, p.sc_b) : ma;
+    launch_any<T>(pair, bn, p, ma, mb, mc, tp, dev, stream);
     return true;
 }
 
