@@ -3,6 +3,8 @@
 // and strided offset calculation.
 #pragma once
 
+#include <utility>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -255,6 +257,40 @@ __device__ __forceinline__ void pack_vec(const float (&in)[V], Vec<__half, V>& v
 inline unsigned blocks_for(int64_t work, int64_t per_block) {
     const int64_t b = (work + per_block - 1) / per_block;
     return static_cast<unsigned>(b < 1 ? 1 : b);
+}
+
+// ------------------------------------------- programmatic dependent launch --
+//
+// Kernels launched with launch_pdl may start while the previous kernel on the
+// stream is finishing: pdl_entry() lets the next kernel launch (its trigger
+// fires once every CTA of this one has started) and then waits until the
+// previous kernel has completed and its memory is visible, before any global
+// access.  The launch and CTA ramp of a kernel overlap its predecessor's last
+// wave; memory ordering is exactly stream order.  Without the launch
+// attribute both instructions are no-ops.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_entry() {
+    pdl_trigger();
+    pdl_wait();
+}
+
+bool pdl_enabled();  // false when TPB200_NO_PDL is set (A/B measurements)
+
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    TPB_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
 }
 
 }  // namespace tpb

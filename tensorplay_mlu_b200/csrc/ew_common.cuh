@@ -321,6 +321,7 @@ struct UnaryBackwardCt {
 template <typename T, int V, int NIN, typename F>
 __global__ void __launch_bounds__(kThreads) ew_contig(T* __restrict__ out, const T* __restrict__ a,
                                                       const T* __restrict__ b, int64_t n, F f) {
+    pdl_entry();
     using C = typename Compute<T>::type;
     using VT = Vec<T, V>;
     const int64_t nvec = n / V;
@@ -370,6 +371,7 @@ __global__ void __launch_bounds__(kThreads) ew_rowbcast(T* __restrict__ out, con
                                                         const T* __restrict__ row, int64_t n,
                                                         FastDiv inner_vecs, uint32_t inner_v,
                                                         bool single, bool row_first, F f) {
+    pdl_entry();
     using C = typename Compute<T>::type;
     using VT = Vec<T, V>;
     const int64_t nvec = n / V;
@@ -413,6 +415,7 @@ template <typename T, int V, bool ROW_FIRST, typename F>
 __global__ void __launch_bounds__(kThreads) ew_rowbcast2d(T* __restrict__ out, const T* __restrict__ full,
                                                           const T* __restrict__ row, int64_t outer,
                                                           int64_t inner_v, F f) {
+    pdl_entry();
     using C = typename Compute<T>::type;
     using VT = Vec<T, V>;
     const int64_t c = int64_t(blockIdx.x) * kThreads + threadIdx.x;
@@ -443,6 +446,7 @@ __global__ void __launch_bounds__(kThreads) ew_rowbcast2d(T* __restrict__ out, c
 template <typename T, int NIN, typename F, typename Calc, typename Index>
 __global__ void __launch_bounds__(kThreads) ew_general(T* out, const T* a, const T* b, Index n,
                                                        Calc calc, F f) {
+    pdl_entry();
     using C = typename Compute<T>::type;
     for (Index i = Index(blockIdx.x) * kThreads + threadIdx.x; i < n;
          i += Index(gridDim.x) * kThreads) {
@@ -472,10 +476,10 @@ void launch_elementwise(const char* what, T* out, const T* a, const T* b, const 
         const bool vec_ok = aligned16(out) && aligned16(a) && (NIN < 2 || aligned16(b));
         if (vec_ok) {
             const unsigned grid = blocks_for(n / V, kThreads * kUnroll);
-            ew_contig<T, V, NIN><<<grid, kThreads, 0, stream>>>(out, a, b, n, fct);
+            launch_pdl(ew_contig<T, V, NIN, Fct>, grid, kThreads, 0, stream, out, a, b, n, fct);
         } else {
             const unsigned grid = blocks_for(n, kThreads * kUnroll);
-            ew_contig<T, 1, NIN><<<grid, kThreads, 0, stream>>>(out, a, b, n, fct);
+            launch_pdl(ew_contig<T, 1, NIN, Fct>, grid, kThreads, 0, stream, out, a, b, n, fct);
         }
         check_launch(what);
         return;
@@ -510,9 +514,9 @@ void launch_elementwise(const char* what, T* out, const T* a, const T* b, const 
                                  static_cast<unsigned>((outer + kRowsPerBlock - 1) / kRowsPerBlock));
                 if (grid2.y <= 65535u) {
                     if (which == 1) {
-                        ew_rowbcast2d<T, V, true><<<grid2, kThreads, 0, stream>>>(out, full, row, outer, iv, fct);
+                        launch_pdl(ew_rowbcast2d<T, V, true, Fct>, grid2, kThreads, 0, stream, out, full, row, outer, iv, fct);
                     } else {
-                        ew_rowbcast2d<T, V, false><<<grid2, kThreads, 0, stream>>>(out, full, row, outer, iv, fct);
+                        launch_pdl(ew_rowbcast2d<T, V, false, Fct>, grid2, kThreads, 0, stream, out, full, row, outer, iv, fct);
                     }
                     check_launch(what);
                     return;
@@ -520,8 +524,8 @@ void launch_elementwise(const char* what, T* out, const T* a, const T* b, const 
             }
             const unsigned grid = blocks_for(n / V, kThreads * kUnroll);
             const uint32_t inner_v = static_cast<uint32_t>(single ? 1 : inner / V);
-            ew_rowbcast<T, V><<<grid, kThreads, 0, stream>>>(out, full, row, n, FastDiv(inner_v),
-                                                            inner_v, single, which == 1, fct);
+            launch_pdl(ew_rowbcast<T, V, Fct>, grid, kThreads, 0, stream, out, full, row, n, FastDiv(inner_v),
+                       inner_v, single, which == 1, fct);
             check_launch(what);
             return;
         }
@@ -531,10 +535,12 @@ void launch_elementwise(const char* what, T* out, const T* a, const T* b, const 
         std::min<int64_t>(blocks_for(n, kThreads), int64_t(num_sms(dev)) * 16));
     if (n < (int64_t(1) << 32)) {
         auto calc = OffsetCalc<NIN + 1>::make(L, which);
-        ew_general<T, NIN><<<grid, kThreads, 0, stream>>>(out, a, b, static_cast<uint32_t>(n), calc, frt);
+        launch_pdl(ew_general<T, NIN, Frt, decltype(calc), uint32_t>, grid, kThreads, 0, stream, out, a, b,
+                   static_cast<uint32_t>(n), calc, frt);
     } else {
         auto calc = OffsetCalc64<NIN + 1>::make(L, which);
-        ew_general<T, NIN><<<grid, kThreads, 0, stream>>>(out, a, b, n, calc, frt);
+        launch_pdl(ew_general<T, NIN, Frt, decltype(calc), int64_t>, grid, kThreads, 0, stream, out, a, b, n, calc,
+                   frt);
     }
     check_launch(what);
 }

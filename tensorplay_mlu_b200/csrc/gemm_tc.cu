@@ -390,6 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    pdl_trigger();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -414,6 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();  // set-up above overlaps the previous kernel; memory access starts here
 
     if (warp == 0) {
         // ---------------------------------------------------- producer --
@@ -685,6 +687,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    pdl_trigger();
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
     const int cluster_id = blockIdx.x >> 1;
@@ -713,6 +716,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();  // set-up above overlaps the previous kernel; memory access starts here
 
     if (warp == 0) {
         // ---------------------------------------------------- producer --
@@ -949,7 +953,7 @@ void launch_tc(const GemmProblem& p, const CUtensorMap& ma, const CUtensorMap& m
     tp.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (uint32_t(tp.a_mn) << 15) |
                (uint32_t(tp.b_mn) << 16) | (uint32_t(BN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
     const int grid = std::min(tp.num_tiles, num_sms(dev));
-    kern<<<grid, kThreads, smem, stream>>>(ma, mb, mc, tp);
+    launch_pdl(kern, grid, kThreads, smem, stream, ma, mb, mc, tp);
     check_launch("gemm_tc");
 }
 
@@ -976,7 +980,7 @@ void launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
     int group_m = static_cast<int>(std::max<int64_t>(1, (int64_t(32) << 20) / std::max<int64_t>(panel, 1)));
     group_m = std::min(group_m, tp.m_tiles);
     const int clusters = std::min(tp.num_tiles, num_sms(dev) / 2);
-    kern<<<2 * clusters, kThreads, smem, stream>>>(ma, mb, mc, tp, group_m);
+    launch_pdl(kern, 2 * clusters, kThreads, smem, stream, ma, mb, mc, tp, group_m);
     check_launch("gemm_tc2");
 }
 

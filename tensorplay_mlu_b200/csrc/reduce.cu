@@ -144,6 +144,7 @@ __global__ void __launch_bounds__(kThreads) reduce_rows(const T* __restrict__ x,
                                                         typename Acc<T>::type* __restrict__ partial,
                                                         OffsetCalc<1> rows_calc, int64_t R, int splits,
                                                         double count, unsigned* __restrict__ ticket) {
+    pdl_entry();
     using A = typename Acc<T>::type;
     constexpr int V = VecWidth<T>::value;
     using VT = Vec<T, V>;
@@ -222,6 +223,7 @@ template <typename T, typename To, int OP>
 __global__ void __launch_bounds__(kThreads) reduce_rows_warp(const T* __restrict__ x, To* __restrict__ out,
                                                              OffsetCalc<1> rows_calc, int64_t rows,
                                                              int64_t R, double count) {
+    pdl_entry();
     using A = typename Acc<T>::type;
     constexpr int V = VecWidth<T>::value;
     using VT = Vec<T, V>;
@@ -389,6 +391,7 @@ template <typename A, typename To, int OP>
 __global__ void __launch_bounds__(kThreads) reduce_row_partials(const A* __restrict__ partial,
                                                                 To* __restrict__ out, int splits,
                                                                 double count) {
+    pdl_entry();
     const int64_t row = blockIdx.x;
     A acc = identity<A, OP>();
     for (int s = threadIdx.x; s < splits; s += kThreads) {
@@ -409,6 +412,7 @@ __global__ void __launch_bounds__(kThreads) reduce_cols(const T* __restrict__ x,
                                                         typename Acc<T>::type* __restrict__ partial,
                                                         int64_t O, int64_t R, int64_t K, int64_t os,
                                                         int64_t rs, double count) {
+    pdl_entry();
     using A = typename Acc<T>::type;
     using VT = Vec<T, V>;
     const int64_t kv = int64_t(blockIdx.x) * kThreads + threadIdx.x;
@@ -457,6 +461,7 @@ template <typename A, typename To, int OP>
 __global__ void __launch_bounds__(kThreads) reduce_col_partials(const A* __restrict__ partial,
                                                                 To* __restrict__ out, int64_t n,
                                                                 int splits, double count) {
+    pdl_entry();
     // Block = 32 columns x 8 split lanes: lane y combines splits y, y+8, ...
     // (two independent chains), then lane 0 combines the 8 lane results in
     // order -- a fixed order, so results are deterministic.
@@ -597,6 +602,7 @@ __device__ __forceinline__ void softmax_row(const T* __restrict__ xr, T* __restr
 template <typename T, int V, int VPT, int THREADS, bool LOG>
 __global__ void __launch_bounds__(THREADS) softmax_rows_reg(const T* __restrict__ x, T* __restrict__ y,
                                                             int64_t D) {
+    pdl_entry();
     const int64_t row = blockIdx.x;
     softmax_row<T, V, VPT, THREADS, LOG>(x + row * D, y + row * D, D, [] {});
 }
@@ -615,6 +621,7 @@ constexpr int kErrSoftmaxRing = 0x7c11;
 template <typename T, int V, int VPT, int THREADS, bool LOG>
 __global__ void __launch_bounds__(THREADS) softmax_rows_ring(const T* __restrict__ x, T* __restrict__ y,
                                                              int64_t rows, int64_t D, int stages, int* err) {
+    pdl_entry();
     extern __shared__ __align__(128) unsigned char ring[];
     __shared__ __align__(8) uint64_t full[kMaxRingStages];
     __shared__ volatile int gave_up;
@@ -741,6 +748,7 @@ __global__ void __launch_bounds__(kThreads) softmax_cols(const T* __restrict__ x
 template <typename T, int V, int VPT, int THREADS>
 __global__ void __launch_bounds__(THREADS) softmax_bwd_rows_reg(const T* __restrict__ dy, const T* __restrict__ y,
                                                                 T* __restrict__ dx, int64_t D, bool log) {
+    pdl_entry();
     using C = typename Compute<T>::type;
     using VT = Vec<T, V>;
     const int64_t row = blockIdx.x;
@@ -895,15 +903,15 @@ void launch_cols(bool vec, const T* x, To* o, typename Acc<T>::type* partial, in
     constexpr int V = VecWidth<T>::value;
     dim3 grid(static_cast<unsigned>(kblocks), static_cast<unsigned>(O), static_cast<unsigned>(splits));
     if (vec) {
-        reduce_cols<T, To, OP, V><<<grid, kThreads, 0, stream>>>(x, o, partial, O, R, K, os, rs, count);
+        launch_pdl(reduce_cols<T, To, OP, V>, grid, kThreads, 0, stream, x, o, partial, O, R, K, os, rs, count);
     } else {
-        reduce_cols<T, To, OP, 1><<<grid, kThreads, 0, stream>>>(x, o, partial, O, R, K, os, rs, count);
+        launch_pdl(reduce_cols<T, To, OP, 1>, grid, kThreads, 0, stream, x, o, partial, O, R, K, os, rs, count);
     }
     check_launch("reduce_cols");
     if (splits > 1) {
         const int64_t n = O * K;
         const unsigned g2 = static_cast<unsigned>((n + 31) / 32);
-        reduce_col_partials<A, To, OP><<<g2, kThreads, 0, stream>>>(partial, o, n, splits, count);
+        launch_pdl(reduce_col_partials<A, To, OP>, g2, kThreads, 0, stream, partial, o, n, splits, count);
         check_launch("reduce_col_partials");
     }
 }
@@ -1010,7 +1018,7 @@ void launch_rows(const RowPlan& p, const T* x, To* o, typename Acc<T>::type* par
     if (p.kind == kRowsWarp) {
         const unsigned grid = static_cast<unsigned>(
             std::min<int64_t>((rows + kWarpsPerBlock - 1) / kWarpsPerBlock, int64_t(sms) * 8));
-        reduce_rows_warp<T, To, OP><<<grid, kThreads, 0, stream>>>(x, o, calc, rows, R, count);
+        launch_pdl(reduce_rows_warp<T, To, OP>, grid, kThreads, 0, stream, x, o, calc, rows, R, count);
         check_launch("reduce_rows_warp");
         return;
     }
@@ -1031,14 +1039,14 @@ void launch_rows(const RowPlan& p, const T* x, To* o, typename Acc<T>::type* par
         check_launch("reduce_rows_ring");
     } else {
         unsigned* ticket = rows == 1 && p.splits > 1 ? reduce_ticket(dev, stream) : nullptr;
-        reduce_rows<T, To, OP><<<static_cast<unsigned>(rows * p.splits), kThreads, 0, stream>>>(
-            x, o, partial, calc, R, p.splits, count, ticket);
+        launch_pdl(reduce_rows<T, To, OP>, static_cast<unsigned>(rows * p.splits), kThreads, 0, stream, x, o, partial,
+                   calc, R, p.splits, count, ticket);
         check_launch("reduce_rows");
         if (ticket != nullptr) return;
     }
     if (p.splits > 1) {
-        reduce_row_partials<A, To, OP><<<static_cast<unsigned>(rows), kThreads, 0, stream>>>(
-            partial, o, p.splits, count);
+        launch_pdl(reduce_row_partials<A, To, OP>, static_cast<unsigned>(rows), kThreads, 0, stream, partial, o,
+                   p.splits, count);
         check_launch("reduce_row_partials");
     }
 }
@@ -1194,7 +1202,7 @@ void launch_ring(T* y, const T* x, int64_t rows, int64_t D, int dev, cudaStream_
         nb = std::max(n, 1);
     }
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(rows, int64_t(num_sms(dev)) * nb));
-    kern<<<grid, THREADS, smem, stream>>>(x, y, rows, D, stages, device_error_word(dev));
+    launch_pdl(kern, grid, THREADS, smem, stream, x, y, rows, D, stages, device_error_word(dev));
     check_launch("softmax_rows_ring");
 }
 
@@ -1214,12 +1222,12 @@ void softmax_rows_launch(T* y, const T* x, int64_t rows, int64_t D, int dev, cud
         return;
     }
     if (vec && nv <= 2048) {
-        if (nv <= 256) softmax_rows_reg<T, V, 1, 256, LOG><<<grid, 256, 0, stream>>>(x, y, D);
-        else if (nv <= 512) softmax_rows_reg<T, V, 2, 256, LOG><<<grid, 256, 0, stream>>>(x, y, D);
-        else if (nv <= 1024) softmax_rows_reg<T, V, 4, 256, LOG><<<grid, 256, 0, stream>>>(x, y, D);
-        else softmax_rows_reg<T, V, 4, 512, LOG><<<grid, 512, 0, stream>>>(x, y, D);
+        if (nv <= 256) launch_pdl(softmax_rows_reg<T, V, 1, 256, LOG>, grid, 256, 0, stream, x, y, D);
+        else if (nv <= 512) launch_pdl(softmax_rows_reg<T, V, 2, 256, LOG>, grid, 256, 0, stream, x, y, D);
+        else if (nv <= 1024) launch_pdl(softmax_rows_reg<T, V, 4, 256, LOG>, grid, 256, 0, stream, x, y, D);
+        else launch_pdl(softmax_rows_reg<T, V, 4, 512, LOG>, grid, 512, 0, stream, x, y, D);
     } else if (!vec && D <= 1024) {
-        softmax_rows_reg<T, 1, 4, 256, LOG><<<grid, 256, 0, stream>>>(x, y, D);
+        launch_pdl(softmax_rows_reg<T, 1, 4, 256, LOG>, grid, 256, 0, stream, x, y, D);
     } else {
         softmax_rows_online<T><<<grid, kThreads, 0, stream>>>(x, y, D, LOG);
     }
@@ -1256,13 +1264,13 @@ void softmax_bwd_launch(bool log, T* dx, const T* dy, const T* y, int64_t outer,
     const bool vec = D % V == 0 && aligned16(dx) && aligned16(dy) && aligned16(y);
     if (vec) {
         const int64_t nv = D / V;
-        if (nv <= 256) softmax_bwd_rows_reg<T, V, 1, 256><<<rows, 256, 0, stream>>>(dy, y, dx, D, log);
-        else if (nv <= 512) softmax_bwd_rows_reg<T, V, 2, 256><<<rows, 256, 0, stream>>>(dy, y, dx, D, log);
-        else if (nv <= 1024) softmax_bwd_rows_reg<T, V, 4, 256><<<rows, 256, 0, stream>>>(dy, y, dx, D, log);
-        else if (nv <= 2048) softmax_bwd_rows_reg<T, V, 4, 512><<<rows, 512, 0, stream>>>(dy, y, dx, D, log);
+        if (nv <= 256) launch_pdl(softmax_bwd_rows_reg<T, V, 1, 256>, rows, 256, 0, stream, dy, y, dx, D, log);
+        else if (nv <= 512) launch_pdl(softmax_bwd_rows_reg<T, V, 2, 256>, rows, 256, 0, stream, dy, y, dx, D, log);
+        else if (nv <= 1024) launch_pdl(softmax_bwd_rows_reg<T, V, 4, 256>, rows, 256, 0, stream, dy, y, dx, D, log);
+        else if (nv <= 2048) launch_pdl(softmax_bwd_rows_reg<T, V, 4, 512>, rows, 512, 0, stream, dy, y, dx, D, log);
         else softmax_bwd_rows_loop<T><<<rows, kThreads, 0, stream>>>(dy, y, dx, D, log);
     } else if (D <= 1024) {
-        softmax_bwd_rows_reg<T, 1, 4, 256><<<rows, 256, 0, stream>>>(dy, y, dx, D, log);
+        launch_pdl(softmax_bwd_rows_reg<T, 1, 4, 256>, rows, 256, 0, stream, dy, y, dx, D, log);
     } else {
         softmax_bwd_rows_loop<T><<<rows, kThreads, 0, stream>>>(dy, y, dx, D, log);
     }

@@ -9,6 +9,8 @@
 
 #include <cuda_runtime.h>
 
+#include <cstdlib>
+
 #include <algorithm>
 #include <array>
 #include <atomic>
@@ -36,6 +38,10 @@ std::atomic<int64_t> g_launches{0};
 }  // namespace
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+bool pdl_enabled() {
+    static const bool on = std::getenv("TPB200_NO_PDL") == nullptr;
+    return on;
+}
 void count_launches(int64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 void uncount_launches(int64_t n) { g_launches.fetch_sub(n, std::memory_order_relaxed); }
 
