@@ -212,14 +212,18 @@ def time_events(fn, iters: int, warmup: int = 3) -> float:
     return start.elapsed_time(end) / iters
 
 
-def op_sweep(ops, hbm_peak: float, iters: int = 10):
-    """memory-bound kernels, achieved GB/s and fraction of HBM."""
+def op_sweep(ops, hbm_peak: float, iters: int = 10, repeats: int = 3):
+    """memory-bound kernels, achieved GB/s and fraction of HBM.
+
+    Each kernel is timed `repeats` times over `iters` back-to-back launches
+    (CUDA events around each run) and the median run is reported, so one
+    disturbed run does not set the figure."""
     g = torch.Generator(device="cuda").manual_seed(0)
     res = {}
     _time_events = globals()["time_events"]
 
     def time_events(fn, n):  # noqa: F811 -- the sweep's own iteration count
-        return _time_events(fn, iters)
+        return statistics.median(_time_events(fn, iters) for _ in range(repeats))
 
     def record(name, ms, nbytes):
         gbs = nbytes / (ms * 1e-3) / 1e9
@@ -271,6 +275,48 @@ def op_sweep(ops, hbm_peak: float, iters: int = 10):
     record("sum_dim0_8192x16384_bf16", time_events(lambda: ops.sum_dim_IntList(hb, [0]), 10),
            (8192 * 16384 + 16384) * 2)
     return res
+
+
+def quick_start(ops, iters: int = 200):
+    """BASELINE config 1, the README quick-start chain on fp32 [256, 256]:
+    y = x @ w; z = relu(y).softmax(-1); loss = z.sum(); backward to x and w.
+    Latency-bound: milliseconds per chain run eagerly (one launch per
+    operator) and replayed from one recording (graph.py's Graph)."""
+    from tensorplay_mlu_b200 import _native as N
+    from tensorplay_mlu_b200.graph import Graph
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(256, 256, generator=g, device="cuda")
+    w = torch.randn(256, 256, generator=g, device="cuda")
+    ones = ops.fill_(torch.empty_like(x), 1.0)
+
+    def chain():
+        y = ops.mm(x, w)
+        z = ops.softmax(ops.relu(y), -1)
+        loss = ops.sum(z)
+        dr = ops._softmax_backward_data(ones, z, -1, torch.float32)
+        dy = ops.threshold_backward(dr, y, 0.0)
+        return loss, ops.mm(dy, w.t()), ops.mm(x.t(), dy)
+
+    launches0 = N.lib().tp_b200_launch_count()
+    chain()
+    per_chain = N.lib().tp_b200_launch_count() - launches0
+    eager_ms = time_events(chain, iters)
+    t0 = time.perf_counter()
+    for _ in range(iters):
+        chain()
+    torch.cuda.synchronize()
+    eager_wall_ms = (time.perf_counter() - t0) * 1e3 / iters
+    graph = Graph()
+    try:
+        graph.capture(chain)
+        replay_ms = time_events(graph.replay, iters)
+    finally:
+        graph.reset()
+    return {"eager_ms": round(eager_ms, 4), "eager_wall_ms": round(eager_wall_ms, 4),
+            "graph_replay_ms": round(replay_ms, 4), "launches_per_chain": int(per_chain),
+            "note": "fp32 [256,256], forward + backward; eager_ms / graph_replay_ms are CUDA-event "
+                    "times per chain on the stream, eager_wall_ms the host wall clock"}
 
 
 def gemm_set(ops, bf16_peak: float):
@@ -385,6 +431,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         with ClockSampler(local) as extra_clocks:
             pre["op_sweep"] = op_sweep(ops, hbm_peak)
             pre["gemm_set"] = gemm_set(ops, bf16_peak)
+            pre["quick_start"] = quick_start(ops)
         pre["extras_clocks"] = extra_clocks.summary()
         torch.cuda.empty_cache()
         tpb.runtime.empty_cache()
@@ -522,6 +569,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             with ClockSampler(local) as extra_clocks:
                 line["op_sweep"] = op_sweep(ops, hbm_peak)
                 line["gemm_set"] = gemm_set(ops, bf16_peak)
+                line["quick_start"] = quick_start(ops)
             line["extras_clocks"] = extra_clocks.summary()
         cpu_value, threads, _ = cpu_mlp_throughput(2, 1, 16)
         line["cpu_baseline"] = {"value": round(cpu_value, 2), "unit": UNIT, "cores": threads, "kind": "port",
@@ -571,6 +619,9 @@ def run_only(args) -> None:
     elif name == "amax_rows_bf16":
         a = rnd(8192, 8192)
         fn = lambda: ops.amax(a, [-1])
+    elif name == "sum_dim0_bf16":  # the MLP's bias gradient: a column sum
+        a = rnd(8192, 16384)
+        fn = lambda: ops.sum_dim_IntList(a, [0])
     elif name == "softmax_bf16":
         a = rnd(32768, 4096)
         fn = lambda: ops.softmax(a, -1)
@@ -631,7 +682,10 @@ def main() -> None:
 
         tpb.load()
         hbm_peak = peaks()[0]
-        print(json.dumps({"op_sweep": op_sweep(tpb.ops, hbm_peak, iters=args.steps)}), flush=True)
+        with ClockSampler(0) as clocks:
+            sweep = op_sweep(tpb.ops, hbm_peak, iters=args.steps)
+            chain = quick_start(tpb.ops)
+        print(json.dumps({"op_sweep": sweep, "quick_start": chain, "clocks": clocks.summary()}), flush=True)
         return
     if args.warmup < 3:
         args.warmup = 3

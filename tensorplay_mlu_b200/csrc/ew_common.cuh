@@ -110,6 +110,39 @@ __device__ __forceinline__ float phi_narrow(float x) {
     return x >= 0.0f ? 1.0f - h : h;  // NaN x: d, h are NaN
 }
 
+// Two fp32 lanes at once: sm_100's packed FFMA2 / FMUL2 / FADD2 take a
+// register pair and round each lane exactly as the scalar instruction does,
+// so the pair forms below give the scalar forms' results bit for bit with
+// half the floating-point issue slots.
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+
+__device__ __forceinline__ float2 phi_narrow2(float2 x) {
+    const float2 ax = make_float2(fabsf(x.x), fabsf(x.y));
+    float2 d = __ffma2_rn(f2(kPhiA6), ax, f2(kPhiA5));
+    d = __ffma2_rn(d, ax, f2(kPhiA4));
+    d = __ffma2_rn(d, ax, f2(kPhiA3));
+    d = __ffma2_rn(d, ax, f2(kPhiA2));
+    d = __ffma2_rn(d, ax, f2(kPhiA1));
+    d = __ffma2_rn(d, ax, f2(kPhiA0));
+    float2 h;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(h.x) : "f"(d.x));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(h.y) : "f"(d.y));
+    h = __fmul2_rn(h, h);
+    h = __fmul2_rn(h, h);
+    h = __fmul2_rn(h, h);
+    h = __fmul2_rn(h, h);
+    const float2 c = __ffma2_rn(h, f2(-1.0f), f2(1.0f));  // 1 - h, one rounding
+    return make_float2(x.x >= 0.0f ? c.x : h.x, x.y >= 0.0f ? c.y : h.y);
+}
+
+// Functors that also have a two-lane form declare `kPair = true` and a
+// `float2 pair(float2, float2)` member; the dense kernel uses it for even
+// vector widths of fp32 compute.
+template <typename F, typename = void>
+struct PairOf { static constexpr bool value = false; };
+template <typename F>
+struct PairOf<F, std::void_t<decltype(F::kPair)>> { static constexpr bool value = F::kPair; };
+
 template <bool Fast, typename C>
 __device__ __forceinline__ C f_exp(C x) {
     if constexpr (Fast && std::is_same<C, float>::value) return __expf(x);
@@ -304,7 +337,10 @@ struct ScalarCt {
 template <typename C, bool Fast, int OP>
 struct UnaryCt {
     C p;
+    // gelu on 16-bit storage: x * Phi(x) two lanes at a time.
+    static constexpr bool kPair = Fast && std::is_same<C, float>::value && OP == TPB_GELU;
     __device__ __forceinline__ C operator()(C a, C) const { return unary_apply<C, Fast>(OP, a, p); }
+    __device__ __forceinline__ float2 pair(float2 a, float2) const { return __fmul2_rn(a, phi_narrow2(a)); }
 };
 template <typename C, bool Fast, int OP>
 struct UnaryBackwardCt {
@@ -347,8 +383,17 @@ __global__ void __launch_bounds__(kThreads) ew_contig(T* __restrict__ out, const
 #pragma unroll
                 for (int j = 0; j < V; ++j) y[j] = C(0);
             }
+            if constexpr (PairOf<F>::value && V % 2 == 0) {
 #pragma unroll
-            for (int j = 0; j < V; ++j) r[j] = f(x[j], y[j]);
+                for (int j = 0; j < V; j += 2) {
+                    const float2 p = f.pair(make_float2(x[j], x[j + 1]), make_float2(y[j], y[j + 1]));
+                    r[j] = p.x;
+                    r[j + 1] = p.y;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < V; ++j) r[j] = f(x[j], y[j]);
+            }
             VT vo;
             pack_vec(r, vo);
             reinterpret_cast<VT*>(out)[i] = vo;

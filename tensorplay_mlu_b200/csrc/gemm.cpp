@@ -62,6 +62,6 @@ extern "C" int tp_b200_gemm(const tpb_tensor* out, const tpb_tensor* a, const tp
         const int dev = device_of(out->data);
         DeviceGuard guard(dev);
         cudaStream_t s = resolve_stream(stream, dev);
-        if (!gemm_tc(p, dev, s)) gemm_simt(p, s);
+        if (!gemm_tc(p, dev, s)) gemm_simt(p, dev, s);
     });
 }

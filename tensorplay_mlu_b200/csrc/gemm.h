@@ -23,7 +23,7 @@ struct GemmProblem {
     int flags;
 };
 
-void gemm_simt(const GemmProblem& p, cudaStream_t stream);
+void gemm_simt(const GemmProblem& p, int dev, cudaStream_t stream);
 // False when the problem does not fit the tensor-core kernel's constraints
 // (dtype, TMA alignment); nothing has been launched then.
 bool gemm_tc(const GemmProblem& p, int dev, cudaStream_t stream);

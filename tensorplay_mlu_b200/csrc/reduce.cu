@@ -9,8 +9,9 @@
 //     one block per (row, split), 16-byte vector loads, warp-shuffle then
 //     shared-memory block reduction;
 //   * columns: the output index is the contiguous side ([O, R, K] over R);
-//     threads own 16-byte column vectors and walk R, split over blocks when
-//     the output is small;
+//     threads own 16-byte column vectors and walk R; when the output is
+//     small a block holds 8 row lanes (combined in shared memory) and the
+//     rows are split over blocks;
 //   * anything else is first gathered into a [kept, reduced] dense scratch
 //     copy and takes the row kernel.
 // Splits write per-block partials to stream-ordered scratch and a second
@@ -81,6 +82,66 @@ __device__ __forceinline__ A combine(A a, A b) {
     if constexpr (OP == TPB_AMAX) return max_nan(a, b);
     else if constexpr (OP == TPB_AMIN) return min_nan(a, b);
     else return a + b;
+}
+
+// One input element into an accumulator: combine(acc, widen(x)).  Sums of
+// 16-bit floats use sm_100's mixed-precision add (add.rn.f32.bf16 / .f16:
+// the widening is exact and the add rounds once, so the result is that of
+// widen-then-add) -- one instruction instead of two.
+template <typename A, int OP, typename T>
+__device__ __forceinline__ A fold(A acc, T x) {
+    if constexpr (OP == TPB_SUM || OP == TPB_MEAN) {
+        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+            asm("add.rn.f32.bf16 %0, %1, %0;" : "+f"(acc) : "h"(__bfloat16_as_ushort(x)));
+            return acc;
+        } else if constexpr (std::is_same<T, __half>::value) {
+            asm("add.rn.f32.f16 %0, %1, %0;" : "+f"(acc) : "h"(__half_as_ushort(x)));
+            return acc;
+        }
+    }
+    return combine<A, OP>(acc, load_as<A>(x));
+}
+
+// A 16-byte vector into an accumulator, elements in order.  max / min of
+// 16-bit floats fold the vector pairwise in the input type first (exact and
+// NaN-propagating, two lanes per instruction) and widen only the last pair.
+template <typename A, int OP, typename T, int V>
+__device__ __forceinline__ A fold_vec(A acc, const Vec<T, V>& v) {
+    constexpr bool narrow = std::is_same<T, __nv_bfloat16>::value || std::is_same<T, __half>::value;
+    if constexpr ((OP == TPB_AMAX || OP == TPB_AMIN) && narrow && V == 8) {
+        using T2 = typename std::conditional<std::is_same<T, __half>::value, __half2, __nv_bfloat162>::type;
+        const T2* p = reinterpret_cast<const T2*>(v.v);
+        T2 m;
+        if constexpr (OP == TPB_AMAX) m = __hmax2_nan(__hmax2_nan(p[0], p[1]), __hmax2_nan(p[2], p[3]));
+        else m = __hmin2_nan(__hmin2_nan(p[0], p[1]), __hmin2_nan(p[2], p[3]));
+        return combine<A, OP>(combine<A, OP>(acc, load_as<A>(m.x)), load_as<A>(m.y));
+    } else {
+#pragma unroll
+        for (int j = 0; j < V; ++j) acc = fold<A, OP>(acc, v.v[j]);
+        return acc;
+    }
+}
+
+// Four vectors into four accumulators.  Sums interleave the accumulators
+// element by element (four independent add chains in flight); max / min
+// fold each vector pairwise first.
+template <typename A, int OP, typename T, int V>
+__device__ __forceinline__ void fold4(A& a0, A& a1, A& a2, A& a3, const Vec<T, V>& a, const Vec<T, V>& b,
+                                      const Vec<T, V>& c, const Vec<T, V>& d) {
+    if constexpr (OP == TPB_SUM || OP == TPB_MEAN) {
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            a0 = fold<A, OP>(a0, a.v[j]);
+            a1 = fold<A, OP>(a1, b.v[j]);
+            a2 = fold<A, OP>(a2, c.v[j]);
+            a3 = fold<A, OP>(a3, d.v[j]);
+        }
+    } else {
+        a0 = fold_vec<A, OP>(a0, a);
+        a1 = fold_vec<A, OP>(a1, b);
+        a2 = fold_vec<A, OP>(a2, c);
+        a3 = fold_vec<A, OP>(a3, d);
+    }
 }
 
 template <typename A, int OP>
@@ -169,19 +230,9 @@ __global__ void __launch_bounds__(kThreads) reduce_rows(const T* __restrict__ x,
         const VT b = vp[v + S];
         const VT c = vp[v + 2 * S];
         const VT d = vp[v + 3 * S];
-#pragma unroll
-        for (int j = 0; j < V; ++j) {
-            acc0 = combine<A, OP>(acc0, load_as<A>(a.v[j]));
-            acc1 = combine<A, OP>(acc1, load_as<A>(b.v[j]));
-            acc2 = combine<A, OP>(acc2, load_as<A>(c.v[j]));
-            acc3 = combine<A, OP>(acc3, load_as<A>(d.v[j]));
-        }
+        fold4<A, OP>(acc0, acc1, acc2, acc3, a, b, c, d);
     }
-    for (; v < nvec; v += S) {
-        const VT a = vp[v];
-#pragma unroll
-        for (int j = 0; j < V; ++j) acc0 = combine<A, OP>(acc0, load_as<A>(a.v[j]));
-    }
+    for (; v < nvec; v += S) acc0 = fold_vec<A, OP>(acc0, vp[v]);
     if (split == 0) {
         for (int64_t k = head + nvec * V + threadIdx.x; k < R; k += kThreads) {
             acc1 = combine<A, OP>(acc1, load_as<A>(base[k]));
@@ -248,19 +299,9 @@ __global__ void __launch_bounds__(kThreads) reduce_rows_warp(const T* __restrict
             const VT b = vp[v + 32];
             const VT c = vp[v + 64];
             const VT d = vp[v + 96];
-#pragma unroll
-            for (int j = 0; j < V; ++j) {
-                acc0 = combine<A, OP>(acc0, load_as<A>(a.v[j]));
-                acc1 = combine<A, OP>(acc1, load_as<A>(b.v[j]));
-                acc2 = combine<A, OP>(acc2, load_as<A>(c.v[j]));
-                acc3 = combine<A, OP>(acc3, load_as<A>(d.v[j]));
-            }
+            fold4<A, OP>(acc0, acc1, acc2, acc3, a, b, c, d);
         }
-        for (; v < nvec; v += 32) {
-            const VT a = vp[v];
-#pragma unroll
-            for (int j = 0; j < V; ++j) acc1 = combine<A, OP>(acc1, load_as<A>(a.v[j]));
-        }
+        for (; v < nvec; v += 32) acc1 = fold_vec<A, OP>(acc1, vp[v]);
         for (int64_t k = head + nvec * V + lane; k < R; k += 32) {
             acc2 = combine<A, OP>(acc2, load_as<A>(base[k]));
         }
@@ -403,11 +444,14 @@ __global__ void __launch_bounds__(kThreads) reduce_row_partials(const A* __restr
 
 // ----------------------------------------------------- column reduce --
 
-// x viewed as [O, R, K]: offset o*os + r*rs + k (k contiguous).  Grid:
-// (ceil(K / (V*threads)), O, splits).  Split s walks rows s, s + splits, ...
-// (neighbouring splits read neighbouring rows), four rows in flight in two
-// accumulator chains.
-template <typename T, typename To, int OP, int V>
+// x viewed as [O, R, K]: offset o*os + r*rs + k (k contiguous).  A block is
+// CX = kThreads / RL column vectors (V elements each) by RL row lanes; grid
+// (ceil(K / (V * CX)), O, splits).  Row lane l = split * RL + ry of the
+// grid's splits * RL lanes walks rows l, l + lanes, ... (neighbouring lanes
+// read neighbouring rows), four rows in flight in two accumulator chains.
+// With RL > 1 the block's lanes are combined in shared memory in lane
+// order, so each block leaves one partial per column.
+template <typename T, typename To, int OP, int V, int RL>
 __global__ void __launch_bounds__(kThreads) reduce_cols(const T* __restrict__ x, To* __restrict__ out,
                                                         typename Acc<T>::type* __restrict__ partial,
                                                         int64_t O, int64_t R, int64_t K, int64_t os,
@@ -415,38 +459,60 @@ __global__ void __launch_bounds__(kThreads) reduce_cols(const T* __restrict__ x,
     pdl_entry();
     using A = typename Acc<T>::type;
     using VT = Vec<T, V>;
-    const int64_t kv = int64_t(blockIdx.x) * kThreads + threadIdx.x;
-    if (kv * V >= K) return;
+    constexpr int CX = kThreads / RL;
+    const int cx = RL == 1 ? static_cast<int>(threadIdx.x) : static_cast<int>(threadIdx.x % CX);
+    const int ry = RL == 1 ? 0 : static_cast<int>(threadIdx.x / CX);
+    const int64_t kv = int64_t(blockIdx.x) * CX + cx;
+    const bool active = kv * V < K;
+    if (RL == 1 && !active) return;
     const int64_t o = blockIdx.y;
     const int split = blockIdx.z;
     const int splits = gridDim.z;
-    A acc[V], acc2[V];
+    const int64_t lanes = int64_t(splits) * RL;
+    A acc[V];
 #pragma unroll
-    for (int j = 0; j < V; ++j) acc[j] = acc2[j] = identity<A, OP>();
-    const T* p = x + o * os + kv * V;
-    const int64_t step = int64_t(splits) * rs;
-    int64_t r = split;
-    for (; r + 3 * int64_t(splits) < R; r += 4 * int64_t(splits)) {
-        const T* q = p + r * rs;
-        const VT a = *reinterpret_cast<const VT*>(q);
-        const VT b = *reinterpret_cast<const VT*>(q + step);
-        const VT c = *reinterpret_cast<const VT*>(q + 2 * step);
-        const VT d = *reinterpret_cast<const VT*>(q + 3 * step);
+    for (int j = 0; j < V; ++j) acc[j] = identity<A, OP>();
+    if (active) {
+        // Four rows in flight; the V column accumulators are independent
+        // chains already, so one set of accumulators (fewer registers, more
+        // resident blocks).
+        const T* p = x + o * os + kv * V;
+        const int64_t step = lanes * rs;
+        int64_t r = int64_t(split) * RL + ry;
+        for (; r + 3 * lanes < R; r += 4 * lanes) {
+            const T* q = p + r * rs;
+            const VT a = *reinterpret_cast<const VT*>(q);
+            const VT b = *reinterpret_cast<const VT*>(q + step);
+            const VT c = *reinterpret_cast<const VT*>(q + 2 * step);
+            const VT d = *reinterpret_cast<const VT*>(q + 3 * step);
 #pragma unroll
-        for (int j = 0; j < V; ++j) {
-            acc[j] = combine<A, OP>(acc[j], load_as<A>(a.v[j]));
-            acc2[j] = combine<A, OP>(acc2[j], load_as<A>(b.v[j]));
-            acc[j] = combine<A, OP>(acc[j], load_as<A>(c.v[j]));
-            acc2[j] = combine<A, OP>(acc2[j], load_as<A>(d.v[j]));
+            for (int j = 0; j < V; ++j) acc[j] = fold<A, OP>(acc[j], a.v[j]);
+#pragma unroll
+            for (int j = 0; j < V; ++j) acc[j] = fold<A, OP>(acc[j], b.v[j]);
+#pragma unroll
+            for (int j = 0; j < V; ++j) acc[j] = fold<A, OP>(acc[j], c.v[j]);
+#pragma unroll
+            for (int j = 0; j < V; ++j) acc[j] = fold<A, OP>(acc[j], d.v[j]);
+        }
+        for (; r < R; r += lanes) {
+            const VT a = *reinterpret_cast<const VT*>(p + r * rs);
+#pragma unroll
+            for (int j = 0; j < V; ++j) acc[j] = fold<A, OP>(acc[j], a.v[j]);
         }
     }
-    for (; r < R; r += splits) {
-        const VT a = *reinterpret_cast<const VT*>(p + r * rs);
+    if constexpr (RL > 1) {
+        __shared__ A lane_acc[RL - 1][V][CX];
+        if (ry > 0) {
 #pragma unroll
-        for (int j = 0; j < V; ++j) acc[j] = combine<A, OP>(acc[j], load_as<A>(a.v[j]));
+            for (int j = 0; j < V; ++j) lane_acc[ry - 1][j][cx] = acc[j];
+        }
+        __syncthreads();
+        if (ry != 0 || !active) return;
+#pragma unroll
+        for (int l = 0; l < RL - 1; ++l)
+#pragma unroll
+            for (int j = 0; j < V; ++j) acc[j] = combine<A, OP>(acc[j], lane_acc[l][j][cx]);
     }
-#pragma unroll
-    for (int j = 0; j < V; ++j) acc[j] = combine<A, OP>(acc[j], acc2[j]);
     if (splits == 1) {
 #pragma unroll
         for (int j = 0; j < V; ++j) out[o * K + kv * V + j] = finalize<To, A, OP>(acc[j], count);
@@ -881,37 +947,69 @@ tpb_tensor dense_like(void* data, int dtype, int ndim, const int64_t* sizes) {
 
 // Column kernel: split R over blocks until the device is filled once with
 // resident blocks (at least 16 rows per split, at most 1024 splits).
+// Column-reduce plan.  Enough 256-vector column blocks to fill the device:
+// one row lane per block, no split.  Otherwise blocks of 32 column vectors
+// (one warp per row segment, whole 128-byte lines) by 8 row lanes, and the
+// rows split over `splits` blocks until the device is full; the partials
+// are then about (resident blocks x 32 vectors), whatever K is, instead of
+// growing with K.
+struct ColPlan {
+    int rl;
+    int64_t kblocks;
+    int splits;
+};
+constexpr int kColLanes = 8;
+
 template <typename T, typename To, int OP>
-int col_splits(int64_t base_blocks, int64_t R, int dev, int sms) {
+ColPlan plan_cols(int64_t O, int64_t R, int64_t K, bool vec, int dev, int sms) {
     constexpr int V = VecWidth<T>::value;
     static int blocks_per_sm[64] = {};
     if (blocks_per_sm[dev] == 0) {
         int n = 0;
-        TPB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, reduce_cols<T, To, OP, V>, kThreads, 0));
+        TPB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, reduce_cols<T, To, OP, V, kColLanes>, kThreads, 0));
         blocks_per_sm[dev] = std::max(n, 1);
     }
     const int64_t cap = int64_t(sms) * blocks_per_sm[dev];
-    if (base_blocks >= cap) return 1;
-    const int64_t splits = std::min<int64_t>((cap + base_blocks - 1) / base_blocks, std::max<int64_t>(R / 16, 1));
-    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(splits, 1024)));
+    const int64_t vecs = vec ? K / V : K;
+    ColPlan p{1, (vecs + kThreads - 1) / kThreads, 1};
+    if (p.kblocks * O >= cap) return p;
+    constexpr int CX = kThreads / kColLanes;
+    p.rl = kColLanes;
+    p.kblocks = (vecs + CX - 1) / CX;
+    const int64_t base = p.kblocks * O;
+    if (base >= cap) return p;
+    // Whole waves only: splits * base <= cap.
+    const int64_t splits = std::min<int64_t>(cap / base, std::max<int64_t>(R / (16 * kColLanes), 1));
+    p.splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(splits, 1024)));
+    return p;
 }
 
 template <typename T, typename To, int OP>
-void launch_cols(bool vec, const T* x, To* o, typename Acc<T>::type* partial, int64_t O, int64_t R, int64_t K,
-                 int64_t os, int64_t rs, int64_t kblocks, int splits, double count, cudaStream_t stream) {
+void launch_cols(const ColPlan& plan, bool vec, const T* x, To* o, typename Acc<T>::type* partial, int64_t O,
+                 int64_t R, int64_t K, int64_t os, int64_t rs, double count, cudaStream_t stream) {
     using A = typename Acc<T>::type;
     constexpr int V = VecWidth<T>::value;
-    dim3 grid(static_cast<unsigned>(kblocks), static_cast<unsigned>(O), static_cast<unsigned>(splits));
-    if (vec) {
-        launch_pdl(reduce_cols<T, To, OP, V>, grid, kThreads, 0, stream, x, o, partial, O, R, K, os, rs, count);
+    dim3 grid(static_cast<unsigned>(plan.kblocks), static_cast<unsigned>(O), static_cast<unsigned>(plan.splits));
+    if (plan.rl == 1) {
+        if (vec) {
+            launch_pdl(reduce_cols<T, To, OP, V, 1>, grid, kThreads, 0, stream, x, o, partial, O, R, K, os, rs, count);
+        } else {
+            launch_pdl(reduce_cols<T, To, OP, 1, 1>, grid, kThreads, 0, stream, x, o, partial, O, R, K, os, rs, count);
+        }
     } else {
-        launch_pdl(reduce_cols<T, To, OP, 1>, grid, kThreads, 0, stream, x, o, partial, O, R, K, os, rs, count);
+        if (vec) {
+            launch_pdl(reduce_cols<T, To, OP, V, kColLanes>, grid, kThreads, 0, stream, x, o, partial, O, R, K, os, rs,
+                       count);
+        } else {
+            launch_pdl(reduce_cols<T, To, OP, 1, kColLanes>, grid, kThreads, 0, stream, x, o, partial, O, R, K, os, rs,
+                       count);
+        }
     }
     check_launch("reduce_cols");
-    if (splits > 1) {
+    if (plan.splits > 1) {
         const int64_t n = O * K;
         const unsigned g2 = static_cast<unsigned>((n + 31) / 32);
-        launch_pdl(reduce_col_partials<A, To, OP>, g2, kThreads, 0, stream, partial, o, n, splits, count);
+        launch_pdl(reduce_col_partials<A, To, OP>, g2, kThreads, 0, stream, partial, o, n, plan.splits, count);
         check_launch("reduce_col_partials");
     }
 }
@@ -1085,13 +1183,10 @@ void reduce_launch(const tpb_tensor& out, const tpb_tensor& xin, uint32_t mask, 
         const int64_t os = kept.n == 2 ? kept.strides[0] : 0;
         const int64_t rs = red.strides[0];
         const bool vec = K % V == 0 && rs % V == 0 && os % V == 0 && aligned16(x);
-        const int vw = vec ? V : 1;
-        const int64_t kblocks = (K / vw + kThreads - 1) / kThreads;
         if (O < 65536) {
-            const int splits = col_splits<T, To, OP>(kblocks * O, R, dev, sms);
-            Scratch partial(splits > 1 ? sizeof(A) * splits * O * K : 0, dev, stream);
-            launch_cols<T, To, OP>(vec, x, o, static_cast<A*>(partial.get()), O, R, K, os, rs, kblocks, splits,
-                                   count, stream);
+            const ColPlan plan = plan_cols<T, To, OP>(O, R, K, vec, dev, sms);
+            Scratch partial(plan.splits > 1 ? sizeof(A) * plan.splits * O * K : 0, dev, stream);
+            launch_cols<T, To, OP>(plan, vec, x, o, static_cast<A*>(partial.get()), O, R, K, os, rs, count, stream);
             return;
         }
     }
@@ -1391,13 +1486,11 @@ void reduce_launch_noalloc(const tpb_tensor& out, const tpb_tensor& xin, uint32_
         const int64_t os = kept.n == 2 ? kept.strides[0] : 0;
         const int64_t rs = red.strides[0];
         const bool vec = K % V == 0 && rs % V == 0 && os % V == 0 && aligned16(x);
-        const int vw = vec ? V : 1;
-        const int64_t kblocks = (K / vw + kThreads - 1) / kThreads;
         TPB_CHECK(O < 65536, "reduce_noalloc: %lld outer rows exceed the column kernel's grid",
                   (long long)O);
-        const int splits = col_splits<T, To, OP>(kblocks * O, R, dev, sms);
-        if (splits > 1) check_noalloc_fit(sizeof(A) * splits * O * K);
-        launch_cols<T, To, OP>(vec, x, o, partial, O, R, K, os, rs, kblocks, splits, count, stream);
+        const ColPlan plan = plan_cols<T, To, OP>(O, R, K, vec, dev, sms);
+        if (plan.splits > 1) check_noalloc_fit(sizeof(A) * plan.splits * O * K);
+        launch_cols<T, To, OP>(plan, vec, x, o, partial, O, R, K, os, rs, count, stream);
         return;
     }
     const bool rows_ok = red.n == 0 || (red.n == 1 && red.strides[0] == 1);

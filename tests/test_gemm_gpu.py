@@ -99,6 +99,27 @@ def test_integer_mm_is_exact(ops, dtype):
     assert_equal(ops.mm(dev(ops, a), dev(ops, b)).cpu(), O.gemm(a, b))
 
 
+def test_small_products_split_k_on_cuda_cores(ops):
+    # Products too small to fill the SMs are split along K on the CUDA-core
+    # kernel and the splits combined in order: exact fp32 (the README chain's
+    # 256^3), f64 with alpha / beta and a broadcast addend, integers exactly,
+    # a batch, and transposed views.
+    a, b = rand(256, 256, seed=1), rand(256, 256, seed=2)
+    assert_close(ops.mm(dev(ops, a), dev(ops, b)), O.gemm(a, b), torch.float32, scale=16)
+    assert_close(ops.mm(dev(ops, a.t().contiguous()).t(), dev(ops, b.t().contiguous()).t()),
+                 O.gemm(a, b), torch.float32, scale=16)
+    a, b, c = (rand(40, 3000, dtype=torch.float64, seed=3), rand(3000, 50, dtype=torch.float64, seed=4),
+               rand(50, dtype=torch.float64, seed=5))
+    assert_close(ops.addmm(dev(ops, c), dev(ops, a), dev(ops, b), beta=0.5, alpha=-2.0),
+                 O.gemm(a, b, c, -2.0, 0.5), torch.float64, scale=60)
+    g = torch.Generator().manual_seed(6)
+    ia = torch.randint(-50, 50, (30, 5000), generator=g, dtype=torch.int32)
+    ib = torch.randint(-50, 50, (5000, 20), generator=g, dtype=torch.int32)
+    assert_equal(ops.mm(dev(ops, ia), dev(ops, ib)).cpu(), O.gemm(ia, ib))
+    x, y = rand(3, 64, 700, seed=7), rand(3, 700, 48, seed=8)
+    assert_close(ops.bmm(dev(ops, x), dev(ops, y)), O.gemm(x, y), torch.float32, scale=30)
+
+
 @pytest.mark.parametrize("dtype", FLOATS)
 def test_addmm_bmm_matmul(ops, dtype):
     bias, a, b = rand(23, dtype=dtype), rand(37, 19, dtype=dtype, seed=1), rand(19, 23, dtype=dtype, seed=2)

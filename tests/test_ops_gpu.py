@@ -329,6 +329,23 @@ def test_large_narrow_float_elementwise(ops, dtype):
     d = dev(ops, a)
     assert_close(ops.add_Tensor(d, d), O.binary(O.ADD, a, a), dtype)
     assert_close(ops.sigmoid(d), O.unary(O.SIGMOID, a), dtype)
+    assert_close(ops.gelu(d), O.unary(O.GELU, a), dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_narrow_gelu_over_its_range(ops, dtype):
+    # Both lanes of the packed (two-at-a-time) form and the tail, over the
+    # negative tail where Phi is tiny, zero, the saturated side, inf and NaN.
+    a = torch.linspace(-12, 12, 4001).to(dtype)
+    a = torch.cat([a, torch.tensor([0.0, -0.0, float("inf"), float("-inf"), float("nan"), 1e-6, -1e-6]).to(dtype)])
+    dy = torch.ones_like(a)
+    for got, want in ((host(ops, ops.gelu(dev(ops, a))), O.unary(O.GELU, a)),
+                      (host(ops, ops.gelu_backward(dev(ops, dy), dev(ops, a))),
+                       O.unary_backward(O.GELU_BACKWARD, dy, a))):
+        finite = torch.isfinite(want)
+        assert_close(got[finite], want[finite], dtype)
+        g, w = got[~finite], want[~finite]
+        assert bool(((g == w) | (torch.isnan(g) & torch.isnan(w))).all()), (g, w)
 
 
 # --------------------------------------------------- reductions, softmax --
