@@ -82,6 +82,12 @@ class ClockSampler:
                 ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            # Wait (up to ~5 s) for the first sample, so the sampler is running
+            # before the timed region starts; that sample itself is pre-region.
+            import select
+
+            if select.select([self.proc.stdout], [], [], 5.0)[0]:
+                self.proc.stdout.readline()
         except OSError:
             self.proc = None
         return self
@@ -198,12 +204,19 @@ def run_reference(args, rank: int, world: int) -> None:
 
 # --------------------------------------------------------------- our arm
 
-def time_events(fn, iters: int, warmup: int = 3) -> float:
-    """Mean milliseconds of `fn` over `iters`, CUDA events on the current stream."""
+def time_events(fn, iters: int, warmup: int = 3, preroll: int = 2) -> float:
+    """Mean milliseconds of `fn` over `iters`, CUDA events on the current stream.
+
+    `preroll` calls are queued (not waited for) just before the start event,
+    so the device is busy when the event is reached and the timed calls run
+    back to back, as in a model's step, rather than each run starting on an
+    idle device behind the host's first launch."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(preroll):
+        fn()
     start.record()
     for _ in range(iters):
         fn()
@@ -212,7 +225,7 @@ def time_events(fn, iters: int, warmup: int = 3) -> float:
     return start.elapsed_time(end) / iters
 
 
-def op_sweep(ops, hbm_peak: float, iters: int = 10, repeats: int = 3):
+def op_sweep(ops, hbm_peak: float, iters: int = 20, repeats: int = 3):
     """memory-bound kernels, achieved GB/s and fraction of HBM.
 
     Each kernel is timed `repeats` times over `iters` back-to-back launches

@@ -99,6 +99,14 @@ int tp_b200_take_device_error(int dev);
  * how many of its kernels ran inside a timed region. */
 int64_t tp_b200_launch_count(void);
 /* Replayed recordings add the kernels one replay runs. */
+/* SMs the persistent tensor-core GEMMs launched afterwards on `dev` may
+ * occupy (rounded down to an even count, at least 2; sms <= 0 or >= the
+ * device's count: all).  No reference counterpart: a data-parallel step
+ * lowers it around a GEMM that overlaps a collective, so the collective's
+ * kernels find free SMs instead of delaying the GEMM's statically
+ * scheduled tiles.  Process-wide per device; affects launches, not
+ * kernels already queued. */
+int tp_b200_set_gemm_sm_limit(int dev, int sms);
 
 /* ------------------------------------------------------------------------
  * Normalisation and loss (replaces tensorplay_mlu/csrc/NNKernels.cpp:59-161,

@@ -96,6 +96,7 @@ _SIGNATURES = {
     "tp_b200_last_error": ([], ctypes.c_char_p),
     "tp_b200_take_device_error": ([_I], _I),
     "tp_b200_launch_count": ([], _I64),
+    "tp_b200_set_gemm_sm_limit": ([_I, _I], _I),
     "tp_b200_capture_ready": ([], _I),
     "tp_b200_capture_stats": ([ctypes.POINTER(ctypes.c_int64)], None),
     "tp_b200_capture_begin": ([_I], _I),

@@ -81,6 +81,9 @@ cudaStream_t resolve_stream(void* stream, int dev);
 // the entry points whose reference signature carries no stream (collectives).
 cudaStream_t thread_current_stream(int dev);
 int num_sms(int dev);
+// SMs the persistent tensor-core GEMMs size their grid to on `dev`: all of
+// them unless tp_b200_set_gemm_sm_limit lowered it.
+int gemm_sm_budget(int dev);
 // Per-device word that kernels with bounded waits write a failure code into.
 int* device_error_word(int dev);
 

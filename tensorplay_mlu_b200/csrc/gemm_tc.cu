@@ -952,7 +952,7 @@ void launch_tc(const GemmProblem& p, const CUtensorMap& ma, const CUtensorMap& m
     const uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : std::is_same<T, float>::value ? 2u : 0u;
     tp.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (uint32_t(tp.a_mn) << 15) |
                (uint32_t(tp.b_mn) << 16) | (uint32_t(BN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
-    const int grid = std::min(tp.num_tiles, num_sms(dev));
+    const int grid = std::min(tp.num_tiles, gemm_sm_budget(dev));
     launch_pdl(kern, grid, kThreads, smem, stream, ma, mb, mc, tp);
     check_launch("gemm_tc");
 }
@@ -979,7 +979,7 @@ void launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
     const int64_t panel = int64_t(kPairBM) * tp.K * int64_t(sizeof(T));
     int group_m = static_cast<int>(std::max<int64_t>(1, (int64_t(32) << 20) / std::max<int64_t>(panel, 1)));
     group_m = std::min(group_m, tp.m_tiles);
-    const int clusters = std::min(tp.num_tiles, num_sms(dev) / 2);
+    const int clusters = std::min(tp.num_tiles, gemm_sm_budget(dev) / 2);
     launch_pdl(kern, 2 * clusters, kThreads, smem, stream, ma, mb, mc, tp, group_m);
     check_launch("gemm_tc2");
 }
@@ -1091,7 +1091,7 @@ bool gemm_tc_typed(const GemmProblem& p_in, int dev, cudaStream_t stream, CUtens
     if (!tma_ok(p.a, es, a_k ? p.sa_m : p.sa_k, p.batch, p.sa_b)) return false;
     if (!tma_ok(p.b, es, b_k ? p.sb_n : p.sb_k, p.batch, p.sb_b)) return false;
     if (p.M >= (int64_t(1) << 31) || p.N >= (int64_t(1) << 31) || p.K >= (int64_t(1) << 31)) return false;
-    const int sms = num_sms(dev);
+    const int sms = gemm_sm_budget(dev);
     const bool pair = use_pair_kernel(p);
     const int bn = pair ? 128 : choose_bn(p.M, p.N, p.batch, sms);  // B rows staged per CTA
     constexpr int kEPR = 128 / es;

@@ -33,6 +33,8 @@ std::array<std::atomic<int*>, kMaxDevices> g_error_words{};
 std::mutex g_error_lock;
 
 std::array<std::atomic<int>, kMaxDevices> g_sms{};
+// SMs the persistent GEMM kernels may occupy per device (0: all of them).
+std::array<std::atomic<int>, kMaxDevices> g_gemm_sms{};
 std::atomic<int64_t> g_launches{0};
 
 }  // namespace
@@ -104,6 +106,12 @@ int num_sms(int dev) {
         g_sms[dev].store(n, std::memory_order_relaxed);
     }
     return n;
+}
+
+int gemm_sm_budget(int dev) {
+    const int all = num_sms(dev);
+    const int limit = g_gemm_sms[dev].load(std::memory_order_relaxed);
+    return limit > 0 && limit < all ? limit : all;
 }
 
 DeviceGuard::DeviceGuard(int dev) : prev_(0), cur_(dev) {
@@ -330,6 +338,16 @@ int tp_b200_mem_get_info(int dev, size_t* free_bytes, size_t* total_bytes) {
 }
 
 int64_t tp_b200_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int tp_b200_set_gemm_sm_limit(int dev, int sms) {
+    return guarded([&] {
+        TPB_CHECK(dev >= 0 && dev < kMaxDevices, "set_gemm_sm_limit: device %d out of range", dev);
+        const int all = num_sms(dev);
+        // An even count (the pair kernel runs 2-SM clusters), at least one pair.
+        const int v = sms <= 0 || sms >= all ? 0 : std::max(2, sms & ~1);
+        g_gemm_sms[dev].store(v, std::memory_order_relaxed);
+    });
+}
 
 int tp_b200_take_device_error(int dev) {
     int value = 0;

@@ -13,7 +13,8 @@ kernels end to end.
 Data parallelism (one rank per GPU): gradients live in one flat buffer split
 into two buckets in backward order, (dW2, db2) then (dW1, db1).  Each bucket
 is all-reduced (SUM) on a side stream as soon as backward has produced it,
-so the first exchange overlaps the dh / dW1 GEMMs; the AVG's 1/world scale is
+so the first exchange overlaps the dh / dW1 GEMMs (the GEMM running beside
+it leaves `comm_sms` SMs to the collective's kernels); the AVG's 1/world scale is
 folded into the SGD step (p -= lr/world * g_sum), not launched as its own
 pass as tensorplay_mlu/distributed.py:241-242 does.
 """
@@ -21,6 +22,7 @@ pass as tensorplay_mlu/distributed.py:241-242 does.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import Optional
 
@@ -41,6 +43,11 @@ class MLPConfig:
     # all-reduced in this many row slices, so each slice's exchange overlaps
     # the next slice's GEMM.
     dw1_slices: int = 1
+    # Data-parallel: SMs left free for the collective's kernels while the
+    # d_a GEMM overlaps the first bucket's all-reduce (the GEMM is persistent
+    # with statically scheduled tiles, so SMs taken by the collective would
+    # otherwise delay its last tiles).  0: the GEMM takes every SM.
+    comm_sms: int = 32
 
 
 def init_params_host(cfg: MLPConfig, seed: int = 0):
@@ -93,6 +100,10 @@ class DataParallelMLP:
         self.dw1 = self.bucket_b.narrow(0, 0, H * D).view(H, D)
         self.db1 = self.bucket_b.narrow(0, H * D, H)
         self.comm_stream = torch.cuda.Stream(device=dev) if pg is not None and self.world > 1 else None
+        # TPB200_COMM_SMS overrides cfg.comm_sms (A/B measurements).
+        reserve = int(os.environ.get("TPB200_COMM_SMS", cfg.comm_sms))
+        total = torch.cuda.get_device_properties(dev).multi_processor_count
+        self._overlap_sms = total - reserve if self.comm_stream is not None and 0 < reserve < total else 0
         # When a list, every GEMM of the step appends a (start, end) pair of
         # CUDA events recorded around its launch on the current stream.
         self.gemm_events: Optional[list] = None
@@ -125,6 +136,9 @@ class DataParallelMLP:
                                        N.stream_of(x.device)), "sum")
         return out
 
+    def _gemm_sm_limit(self, sms: int) -> None:
+        N.check(N.lib().tp_b200_set_gemm_sm_limit(self.device.index, sms), "set_gemm_sm_limit")
+
     def _allreduce_async(self, bucket, ready_event):
         """SUM all-reduce of ``bucket`` on the comm stream after ``ready_event``."""
         self.comm_stream.wait_event(ready_event)
@@ -150,7 +164,14 @@ class DataParallelMLP:
             ev = torch.cuda.Event()
             ev.record()
             work_a = self._allreduce_async(self.bucket_a, ev)
-        d_a = self._timed(ops.mm, d_out, self.w2)
+        if self._overlap_sms:
+            self._gemm_sm_limit(self._overlap_sms)
+            try:
+                d_a = self._timed(ops.mm, d_out, self.w2)
+            finally:
+                self._gemm_sm_limit(0)
+        else:
+            d_a = self._timed(ops.mm, d_out, self.w2)
         d_h = ops.gelu_backward(d_a, h)
         if self.comm_stream is None:
             self._timed(self._mm_into, self.dw1, d_h.t(), x)

@@ -99,6 +99,26 @@ def test_integer_mm_is_exact(ops, dtype):
     assert_equal(ops.mm(dev(ops, a), dev(ops, b)).cpu(), O.gemm(a, b))
 
 
+def test_gemm_sm_limit_changes_the_grid_not_the_result(ops, backend):
+    # Each output tile is computed the same way whichever CTA takes it, so a
+    # lower SM budget (fewer persistent CTAs / pairs) gives identical bits,
+    # for the CTA-pair kernel (1024 x 768) and the 1-SM kernel (200 x 300).
+    lib = backend._native.lib()
+    device = torch.cuda.current_device()
+    cases = [(rand(1024, 512, dtype=torch.bfloat16, seed=1), rand(512, 768, dtype=torch.bfloat16, seed=2)),
+             (rand(200, 256, dtype=torch.bfloat16, seed=3), rand(256, 300, dtype=torch.bfloat16, seed=4))]
+    for a, b in cases:
+        want = ops.to_host(ops.mm(dev(ops, a), dev(ops, b)))
+        for sms in (2, 10, 37, 132):
+            assert lib.tp_b200_set_gemm_sm_limit(device, sms) == 0
+            try:
+                got = ops.to_host(ops.mm(dev(ops, a), dev(ops, b)))
+            finally:
+                assert lib.tp_b200_set_gemm_sm_limit(device, 0) == 0
+            assert_equal(got, want)
+    assert lib.tp_b200_set_gemm_sm_limit(-1, 8) != 0
+
+
 def test_small_products_split_k_on_cuda_cores(ops):
     # Products too small to fill the SMs are split along K on the CUDA-core
     # kernel and the splits combined in order: exact fp32 (the README chain's
