@@ -225,22 +225,36 @@ def time_events(fn, iters: int, warmup: int = 3, preroll: int = 2) -> float:
     return start.elapsed_time(end) / iters
 
 
-def op_sweep(ops, hbm_peak: float, iters: int = 20, repeats: int = 3):
+def op_sweep(ops, hbm_peak: float, iters: int = 20, passes: int = 3):
     """memory-bound kernels, achieved GB/s and fraction of HBM.
 
-    Each kernel is timed `repeats` times over `iters` back-to-back launches
-    (CUDA events around each run) and the median run is reported, so one
-    disturbed run does not set the figure."""
+    The whole sweep runs `passes` times; each kernel is timed over `iters`
+    back-to-back launches (CUDA events) per pass and its median pass is
+    reported, with `spread` = slowest / fastest pass.  Passes are seconds
+    apart, so a disturbance of the device that lasts a while spoils one pass
+    of a row, not its figure."""
+    runs = [_op_sweep_pass(ops, iters) for _ in range(passes)]
+    res = {}
+    for name in runs[0]:
+        times = sorted(r[name][0] for r in runs)
+        ms, nbytes = statistics.median(times), runs[0][name][1]
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res[name] = {"ms": round(ms, 4), "gb_s": round(gbs, 1), "frac": round(gbs / hbm_peak, 3),
+                     "spread": round(times[-1] / times[0], 2)}
+    return res
+
+
+def _op_sweep_pass(ops, iters: int):
+    """One pass of the sweep: {row: (ms per launch, algorithmic bytes)}."""
     g = torch.Generator(device="cuda").manual_seed(0)
     res = {}
     _time_events = globals()["time_events"]
 
     def time_events(fn, n):  # noqa: F811 -- the sweep's own iteration count
-        return statistics.median(_time_events(fn, iters) for _ in range(repeats))
+        return _time_events(fn, iters)
 
     def record(name, ms, nbytes):
-        gbs = nbytes / (ms * 1e-3) / 1e9
-        res[name] = {"ms": round(ms, 4), "gb_s": round(gbs, 1), "frac": round(gbs / hbm_peak, 3)}
+        res[name] = (ms, nbytes)
 
     M = N = 8192
     for dt, tag in ((torch.float32, "f32"), (torch.bfloat16, "bf16")):
