@@ -232,7 +232,18 @@ __global__ void __launch_bounds__(kThreads) reduce_rows(const T* __restrict__ x,
         const VT d = vp[v + 3 * S];
         fold4<A, OP>(acc0, acc1, acc2, acc3, a, b, c, d);
     }
-    for (; v < nvec; v += S) acc0 = fold_vec<A, OP>(acc0, vp[v]);
+    // The last (at most three) vectors of this thread, loaded together
+    // rather than one round trip each.
+    if (v < nvec) {
+        const bool h1 = v + S < nvec, h2 = v + 2 * S < nvec;
+        const VT a = vp[v];
+        VT b, c;
+        if (h1) b = vp[v + S];
+        if (h2) c = vp[v + 2 * S];
+        acc0 = fold_vec<A, OP>(acc0, a);
+        if (h1) acc1 = fold_vec<A, OP>(acc1, b);
+        if (h2) acc2 = fold_vec<A, OP>(acc2, c);
+    }
     if (split == 0) {
         for (int64_t k = head + nvec * V + threadIdx.x; k < R; k += kThreads) {
             acc1 = combine<A, OP>(acc1, load_as<A>(base[k]));
@@ -301,7 +312,17 @@ __global__ void __launch_bounds__(kThreads) reduce_rows_warp(const T* __restrict
             const VT d = vp[v + 96];
             fold4<A, OP>(acc0, acc1, acc2, acc3, a, b, c, d);
         }
-        for (; v < nvec; v += 32) acc1 = fold_vec<A, OP>(acc1, vp[v]);
+        // The last (at most three) vectors, loaded together.
+        if (v < nvec) {
+            const bool h1 = v + 32 < nvec, h2 = v + 64 < nvec;
+            const VT a = vp[v];
+            VT b, c;
+            if (h1) b = vp[v + 32];
+            if (h2) c = vp[v + 64];
+            acc1 = fold_vec<A, OP>(acc1, a);
+            if (h1) acc2 = fold_vec<A, OP>(acc2, b);
+            if (h2) acc3 = fold_vec<A, OP>(acc3, c);
+        }
         for (int64_t k = head + nvec * V + lane; k < R; k += 32) {
             acc2 = combine<A, OP>(acc2, load_as<A>(base[k]));
         }
@@ -1310,8 +1331,14 @@ void softmax_rows_launch(T* y, const T* x, int64_t rows, int64_t D, int dev, cud
     const bool vec = D % V == 0 && aligned16(x) && aligned16(y);
     const int64_t nv = D / V;
     if (vec && nv <= 2048 && use_softmax_ring(sizeof(T), rows, dev)) {
+        // 4096-wide 16-bit rows: 128-thread blocks, 32 elements per thread.
+        // Same-box A/B ([32768, 4096] bf16, six ring stages): 128 threads
+        // 0.87-0.89 of the HBM copy peak, 256 threads 0.81-0.83, 512
+        // threads 0.64 -- the per-row block reductions' barriers, not
+        // occupancy, set the rate; shallower rings (3-4 stages) lost
+        // whatever the block size.
         if (nv <= 256) launch_ring<T, V, 1, 256, LOG>(y, x, rows, D, dev, stream);
-        else if (nv <= 512) launch_ring<T, V, 2, 256, LOG>(y, x, rows, D, dev, stream);
+        else if (nv <= 512) launch_ring<T, V, 4, 128, LOG>(y, x, rows, D, dev, stream);
         else if (nv <= 1024) launch_ring<T, V, 4, 256, LOG>(y, x, rows, D, dev, stream);
         else launch_ring<T, V, 4, 512, LOG>(y, x, rows, D, dev, stream);
         return;
