@@ -1,0 +1,35 @@
+"""bench.py's host-side logic: the op sweep's median over full passes and
+its spread figure, and the clock summary's throttle reasons (no GPU)."""
+
+from __future__ import annotations
+
+import bench
+
+
+def test_op_sweep_reports_the_median_pass_and_its_spread(monkeypatch):
+    passes = iter([
+        {"row_a": (1.0, 1e9), "row_b": (2.0, 1e9)},
+        {"row_a": (3.0, 1e9), "row_b": (2.2, 1e9)},   # a disturbed pass of row_a
+        {"row_a": (1.1, 1e9), "row_b": (2.1, 1e9)},
+    ])
+    monkeypatch.setattr(bench, "_op_sweep_pass", lambda ops, iters: next(passes))
+    res = bench.op_sweep(None, hbm_peak=1000.0, iters=20, passes=3)
+    assert res["row_a"]["ms"] == 1.1 and res["row_a"]["spread"] == 3.0
+    assert res["row_a"]["gb_s"] == round(1e9 / 1.1e-3 / 1e9, 1)
+    assert res["row_a"]["frac"] == round(1e9 / 1.1e-3 / 1e9 / 1000.0, 3)
+    assert res["row_b"]["ms"] == 2.1 and res["row_b"]["spread"] == 1.1
+
+
+def test_clock_summary_lists_active_throttle_reasons():
+    s = bench.ClockSampler(0)
+    s.lines = [
+        "0, 1965, 1965, 700.0, 0x0, Not Active, Not Active, Not Active, Not Active",
+        "0, 1410, 1965, 1000.0, 0x4, Not Active, Not Active, Not Active, Active",
+        "0, 1380, 1965, 1000.0, 0x4, Not Active, Not Active, Not Active, Active",
+    ]
+    out = s.summary()
+    assert out["sm_mhz"] == 1410 and out["sm_max_mhz"] == 1965
+    assert out["reasons"] == ["sw_power_cap"] and out["samples"] == 3
+    empty = bench.ClockSampler(0)
+    empty.lines = []
+    assert empty.summary()["reasons"] == ["unsampled"]
