@@ -255,6 +255,31 @@ __device__ __forceinline__ void tile_coords(const TcParams& p, int tile, int& b,
     nt = q / gsize;
 }
 
+// v[j] += beta * addend[n_base + j] for one 32-column chunk of a row.  An
+// addend with unit column stride whose chunk lies inside N on a 16-byte
+// boundary is read as 16-byte vectors (for a bias row every lane reads the
+// same address: a broadcast), not element by element; the arithmetic is the
+// same FFMA either way.
+template <typename T>
+__device__ __forceinline__ void add_addend_chunk(const TcParams& p, const T* crow_in, int64_t n_base, float (&v)[32]) {
+    constexpr int kPer = 16 / int(sizeof(T));
+    if (p.sci_n == 1 && n_base + 32 <= p.N && (reinterpret_cast<uintptr_t>(crow_in + n_base) & 15u) == 0) {
+        const Vec<T, kPer>* src = reinterpret_cast<const Vec<T, kPer>*>(crow_in + n_base);
+#pragma unroll
+        for (int q = 0; q < 32 / kPer; ++q) {
+            float f[kPer];
+            unpack_vec(src[q], f);
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) v[q * kPer + j] = fmaf(p.beta, f[j], v[q * kPer + j]);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            if (n_base + j < p.N) v[j] = fmaf(p.beta, load_as<float>(crow_in[(n_base + j) * p.sci_n]), v[j]);
+        }
+    }
+}
+
 // The epilogue of one accumulator: this warp's 32 rows (its TMEM lane
 // quadrant, t_rows = TMEM address of row 0 / column 0 of the accumulator)
 // for columns [col0, col0 + NCOL).  The load of chunk c + 1 is issued before
@@ -278,13 +303,7 @@ __device__ __forceinline__ void store_accumulator(const TcParams& p, uint32_t t_
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(rc[j]);
-            if (cin != nullptr) {
-                const T* crow_in = cin + b * p.sci_b + gm * p.sci_m;
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    if (n_base + j < p.N) v[j] += p.beta * load_as<float>(crow_in[(n_base + j) * p.sci_n]);
-                }
-            }
+            if (cin != nullptr) add_addend_chunk<T>(p, cin + b * p.sci_b + gm * p.sci_m, n_base, v);
             if (p.vec_store && n_base + 32 <= p.N) {
                 constexpr int V = 16 / sizeof(T);
 #pragma unroll
@@ -330,13 +349,7 @@ __device__ __forceinline__ void store_accumulator_tma(const TcParams& p, const C
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(rc[j]);
-        if (cin != nullptr && row_ok) {
-            const T* crow_in = cin + b * p.sci_b + gm * p.sci_m;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                if (n_base + j < p.N) v[j] += p.beta * load_as<float>(crow_in[(n_base + j) * p.sci_n]);
-            }
-        }
+        if (cin != nullptr && row_ok) add_addend_chunk<T>(p, cin + b * p.sci_b + gm * p.sci_m, n_base, v);
         Vec<T, 32> packed;
         pack_vec(v, packed);
         // The previous store from this staging tile has finished reading it.

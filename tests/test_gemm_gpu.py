@@ -157,14 +157,19 @@ def test_addmm_bmm_matmul(ops, dtype):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_addmm_bias_in_epilogue_on_tensor_cores(ops, dtype):
-    M, N, K = 256, 384, 128
+@pytest.mark.parametrize("M,N,K", [(256, 384, 128), (600, 1000, 256), (300, 520, 64)])
+def test_addmm_bias_in_epilogue_on_tensor_cores(ops, dtype, M, N, K):
+    # Whole 32-column chunks read the addend as 16-byte vectors; ragged N
+    # (1000, 520) and an offset (unaligned) bias exercise the element path.
     bias, a, b = rand(N, dtype=dtype), rand(M, K, dtype=dtype, seed=1), rand(K, N, dtype=dtype, seed=2)
     assert_close(ops.addmm(dev(ops, bias), dev(ops, a), dev(ops, b)), O.gemm(a, b, bias, 1.0, 1.0),
                  dtype, scale=K ** 0.5)
     full = rand(M, N, dtype=dtype, seed=3)
     assert_close(ops.addmm(dev(ops, full), dev(ops, a), dev(ops, b), beta=0.25, alpha=-1.0),
                  O.gemm(a, b, full, -1.0, 0.25), dtype, scale=K ** 0.5)
+    wide = rand(N + 1, dtype=dtype, seed=4)
+    assert_close(ops.addmm(dev(ops, wide)[1:], dev(ops, a), dev(ops, b)), O.gemm(a, b, wide[1:], 1.0, 1.0),
+                 dtype, scale=K ** 0.5)
 
 
 @pytest.mark.parametrize("dtype", FLOATS)
