@@ -1294,6 +1294,9 @@ bool use_split_tf32(const GemmProblem& p) {
     if (force != nullptr && std::strcmp(force, "simt") == 0) return false;
     if (3 * p.K >= (int64_t(1) << 31) || p.M >= (int64_t(1) << 31) || p.N >= (int64_t(1) << 31)) return false;
     if (p.batch > 65535) return false;  // the fix-up grids' y extent
+    // An operand broadcast over the batch (batch stride 0) has no batched
+    // tensor map; such products take the CUDA-core kernel, as TF32 ones do.
+    if (p.batch > 1 && (p.sa_b == 0 || p.sb_b == 0)) return false;
     return p.M >= 128 && p.N >= 128 && p.K >= 16 && p.M * p.N * p.K * p.batch >= (int64_t(1) << 27);
 }
 

@@ -232,6 +232,22 @@ class _Highest:
         torch.set_float32_matmul_precision(self.previous)
 
 
+def test_fp32_split_tf32_batches_and_batch_broadcast(ops):
+    # Full-precision batched products: two real batch members on the split-TF32
+    # tensor-core path (bit-identical to the single product), and operands
+    # broadcast over the batch (stride 0), which take the CUDA-core kernel.
+    with _Highest():
+        a, b = rand(384, 3072, seed=21), rand(3072, 320, seed=22)
+        da, db = dev(ops, a), dev(ops, b)
+        one = ops.to_host(ops.mm(da, db))
+        two = ops.to_host(ops.bmm(dev(ops, a.unsqueeze(0).repeat(2, 1, 1)), dev(ops, b.unsqueeze(0).repeat(2, 1, 1))))
+        assert_equal(one, two[0])
+        assert_equal(one, two[1])
+        assert check_sampled(ops.mm(da, db), a, b) <= 1e-5
+        bc = ops.bmm(da.unsqueeze(0).expand(2, -1, -1), db.unsqueeze(0).expand(2, -1, -1))
+        assert check_sampled(bc, a.expand(2, -1, -1), b.expand(2, -1, -1)) <= 1e-5
+
+
 def test_fp32_split_tf32_layouts_and_epilogue(ops):
     # Large enough for the split-TF32 tensor-core path: transposed operands
     # (copied K-major first), an operand broadcast over the batch, and the
