@@ -51,36 +51,91 @@ def peaks():
         return 6650.0, 1590.0, 1400.0, "fallback"
 
 
-def profile_figure(name: str, key: str):
-    """A number recorded in a committed ncu summary under profiles/ (``key: value``)."""
-    path = os.path.join(ROOT, "profiles", name)
-    try:
-        for line in open(path):
-            if line.strip().startswith(key + ":"):
-                return float(line.split(":", 1)[1].split()[0])
-    except OSError:
-        pass
-    return None
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of
+# each of the step's five products, from one ncu capture of the five
+# gemm_tc2_kernel launches of a full-size step (the command and the figures:
+# profiles/gemm_tc2_mlp_step_5_products.md).  Algorithmic bytes per launch:
+# A + B read once, C written once.
+GEMM_NAMES = ("h=xW1^T", "out=aW2^T", "dW2=dout^T a", "da=dout W2", "dW1=dh^T x")
+GEMM_DRAM_BYTES = {
+    "h=xW1^T": 415750400 + 251609088,
+    "out=aW2^T": 1409426432 + 58553856,
+    "dW2=dout^T a": 995802624 + 123874816,
+    "da=dout W2": 425874176 + 247974912,
+    "dW1=dh^T x": 1236060416 + 124142848,
+}
+GEMM_ALGORITHMIC_BYTES = {
+    "h=xW1^T": (8192 * 4096 + 16384 * 4096 + 8192 * 16384 + 16384) * 2,
+    "out=aW2^T": (8192 * 16384 + 4096 * 16384 + 8192 * 4096 + 4096) * 2,
+    "dW2=dout^T a": (8192 * 4096 + 8192 * 16384 + 4096 * 16384) * 2,
+    "da=dout W2": (8192 * 4096 + 4096 * 16384 + 8192 * 16384) * 2,
+    "dW1=dh^T x": (8192 * 16384 + 8192 * 4096 + 16384 * 4096) * 2,
+}
 
 
 # ------------------------------------------------------------------ clocks
 
 class ClockSampler:
-    """nvidia-smi samples during the timed region (SM clock, throttle reasons)."""
+    """SM clock and throttle reasons sampled during the timed region.
+
+    NVML is polled from a thread every 5 ms (the timed regions last from
+    ~0.1 s), the device found by its PCI bus id; nvidia-smi at 20 ms is the
+    fallback where NVML cannot be loaded."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
-    def __init__(self, device: int):
+    def __init__(self, device: int, period_s: float = 0.005):
         self.device = device
+        self.period = period_s
         self.proc = None
+        self.thread = None
+        self.rows = []  # (sm_mhz, max_mhz, [flag per NAMES])
+
+    def _nvml_handle(self):
+        import pynvml
+
+        pynvml.nvmlInit()
+        try:
+            bus = torch.cuda.get_device_properties(self.device).pci_bus_id
+            dom = torch.cuda.get_device_properties(self.device).pci_domain_id
+            dev = torch.cuda.get_device_properties(self.device).pci_device_id
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(f"{dom:08x}:{bus:02x}:{dev:02x}.0")
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device)
 
     def __enter__(self):
+        import threading
+
+        try:
+            nv, handle = self._nvml_handle()
+            bits = [nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                    nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap]
+            max_mhz = nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM)
+            self.stop = threading.Event()
+
+            def poll():
+                while not self.stop.is_set():
+                    try:
+                        mhz = nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM)
+                        reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                        self.rows.append((float(mhz), float(max_mhz), [bool(reasons & b) for b in bits]))
+                    except Exception:
+                        pass
+                    self.stop.wait(self.period)
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            self.source = "nvml"
+            return self
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             # Wait (up to ~5 s) for the first sample, so the sampler is running
             # before the timed region starts; that sample itself is pre-region.
@@ -88,12 +143,16 @@ class ClockSampler:
 
             if select.select([self.proc.stdout], [], [], 5.0)[0]:
                 self.proc.stdout.readline()
+            self.source = "nvidia-smi"
         except OSError:
             self.proc = None
+            self.source = None
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -101,26 +160,29 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+            self.add_smi_lines(out.splitlines())
         return False
 
-    def summary(self):
-        rows = []
-        for line in getattr(self, "lines", []):
+    def add_smi_lines(self, lines):
+        """Samples from nvidia-smi's csv lines (FIELDS, no header, no units)."""
+        for line in lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
             try:
-                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+                self.rows.append((float(parts[1]), float(parts[2]), [f.lower() == "active" for f in parts[5:9]]))
             except ValueError:
                 continue
+
+    def summary(self):
+        rows = list(self.rows)
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags)
-                          if f.lower() == "active"})
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0,
+                    "source": getattr(self, "source", None)}
+        reasons = sorted({self.NAMES[i] for _, _, flags in rows for i, f in enumerate(flags) if f})
         return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(rows)}
+                "sm_mhz_min": min(r[0] for r in rows), "reasons": reasons, "samples": len(rows),
+                "source": self.source}
 
 
 # ----------------------------------------------------------- distributed
@@ -164,12 +226,32 @@ class HostGroup:
 
 # ------------------------------------------------------------- reference arm
 
-def cpu_mlp_throughput(steps: int, warmup: int, rows: int = 16):
-    """The CPU port of the step (oracle/mlp.c) on `rows` sampled rows per step,
-    full-size weights, all host threads.  Returns (samples/s, threads, seconds)."""
+def workload_config(world: int) -> dict:
+    """The `config` object of both arms' lines (identical, so the two arms
+    are the same workload)."""
+    return {"workload": WORKLOAD, "model": "MLP 4096-16384-4096 gelu, MSE loss, SGD lr 1e-3",
+            "global_batch": PER_RANK_BATCH * world, "per_rank_batch": PER_RANK_BATCH, "seq_len": None,
+            "parallelism": f"dp{world}",
+            "l2": "inputs larger than L2 (per-step working set ~1.9 GB > 126 MB)"}
+
+
+def host_threads() -> int:
+    """The host cores this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_mlp_throughput(steps: int, warmup: int, rows: int = PER_RANK_BATCH):
+    """The CPU port of the step (oracle/mlp.c: blocked fp32 products over
+    bf16 tensors) on `rows` rows per step with the full-size weights, on
+    every host core.  Returns (samples/s, threads, seconds, GFLOP/s)."""
     import oracle as O
     from tensorplay_mlu_b200.train import MLPConfig, init_params_host, make_batch_host
 
+    threads = host_threads()
+    O.set_num_threads(threads)  # torchrun exports OMP_NUM_THREADS=1
     cfg = MLPConfig(d_in=D_IN, d_hidden=D_HIDDEN, batch=rows)
     w1, b1, w2, b2 = [p.contiguous() for p in init_params_host(cfg, seed=0)]
     x, t = make_batch_host(cfg, seed=0)
@@ -179,24 +261,28 @@ def cpu_mlp_throughput(steps: int, warmup: int, rows: int = 16):
     for _ in range(steps):
         O.mlp_step(x, t, w1, b1, w2, b2, cfg.lr)
     elapsed = time.perf_counter() - start
-    return rows * steps / elapsed, O.num_threads(), elapsed
+    gflops = 5 * 2.0 * rows * D_IN * D_HIDDEN * steps / elapsed / 1e9
+    return rows * steps / elapsed, O.num_threads(), elapsed, gflops
 
 
 def run_reference(args, rank: int, world: int) -> None:
+    """The reference's CPU path of the step: TensorPlay's CPU kernels are not
+    installable here, so its port (oracle/mlp.c) runs the full 8192-row step
+    on rank 0's host cores; the other ranks exit without work."""
     if rank != 0:
         return
-    rows = 16
-    value, threads, elapsed = cpu_mlp_throughput(args.steps, args.warmup, rows)
+    value, threads, elapsed, gflops = cpu_mlp_throughput(args.steps, args.warmup)
     line = {
         "impl": "reference",
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000.0 * elapsed / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "model": "MLP 4096-16384-4096 gelu, MSE, SGD",
-                   "global_batch": PER_RANK_BATCH * world, "parallelism": f"dp{world}"},
+        "config": workload_config(world),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{rows} rows per step of the 8192-row batch, full 134M-parameter "
-                                   "weights (forward, backward, SGD) -- oracle/mlp.c on the host cores"},
+                         "gflop_s": round(gflops, 1),
+                         "sample": f"the full {PER_RANK_BATCH}-row step (forward, backward, SGD over the "
+                                   "134M-parameter weights), every step; oracle/mlp.c's blocked fp32 products "
+                                   "on the host cores, rank 0 only"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -435,6 +521,22 @@ def collective_sweep(pg, host, ops, world: int, max_bytes: int = 1 << 30):
     return res
 
 
+def h2d_only_ms(upload, copy_stream, steps: int, host) -> float:
+    """Milliseconds per step of the e2e leg's host->device copies alone
+    (both slots' batches, pinned memory, the copy stream), max over ranks."""
+    for slot in (0, 1):
+        upload(slot)
+    copy_stream.synchronize()
+    host.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(copy_stream)
+    for i in range(steps):
+        upload(i % 2)
+    e1.record(copy_stream)
+    e1.synchronize()
+    return host.max(e0.elapsed_time(e1) / steps)
+
+
 def run_ours(args, rank: int, world: int, local: int) -> None:
     import tensorplay_mlu_b200 as tpb
     from tensorplay_mlu_b200 import _native as N
@@ -507,7 +609,9 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     # One pinned slot per step: every step's loss is copied to the host
     # without stalling the host on it (as a training loop logs its loss);
     # the slots are checked once the timed region has ended.
-    loss_host = torch.empty(max(args.steps, args.warmup, 1), dtype=torch.float32).pin_memory()
+    # NaN until a step's copy lands, so a slot that was never written fails
+    # the check after the timed region.
+    loss_host = torch.full((max(args.steps, args.warmup, 1),), float("nan"), dtype=torch.float32).pin_memory()
     loss_keep = []
 
     def upload(slot):
@@ -546,14 +650,34 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     host.barrier()
     read_back = loss_host[:args.steps]
     assert bool(torch.isfinite(read_back).all()), "a step's loss read back from the device is not finite"
+    last_dev = loss_keep[-1].item()
+    assert read_back[-1].item() == last_dev, (read_back[-1].item(), last_dev)
     loss_keep.clear()
+
+    # ---- the end-to-end ceiling: the same per-step host->device copies alone
+    h2d_ms = h2d_only_ms(upload, copy_stream, args.steps, host)
+
+    # ---- data parallelism kept every rank's parameters identical
+    params_identical = None
+    if world > 1:
+        import hashlib
+
+        digest = hashlib.sha256()
+        for p in model.params():
+            digest.update(ops.to_host(p).view(torch.int16).numpy().tobytes())
+        digests = [None] * world
+        host.dist.all_gather_object(digests, digest.hexdigest())
+        params_identical = len(set(digests)) == 1
+        assert params_identical, "data-parallel ranks hold different parameters"
 
     samples = PER_RANK_BATCH * world
     value = samples / (ms * 1e-3)
     e2e_value = samples / (e2e_ms * 1e-3)
     gemm_flops = 2.0 * PER_RANK_BATCH * D_IN * D_HIDDEN
     achieved = gemm_flops / (gemm_avg_ms * 1e-3) / 1e12
-    traffic = profile_figure("gemm_tc2_mlp_8192x16384x4096.md", "dram_bytes_per_launch")
+    traffic_by_gemm = {k: GEMM_DRAM_BYTES.get(k) for k in GEMM_NAMES}
+    known = [v for v in traffic_by_gemm.values() if v is not None]
+    traffic = sum(known) / len(known) if len(known) == len(GEMM_NAMES) else None
 
     line = None
     if rank == 0:
@@ -562,26 +686,31 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: inputs/targets N(0,1) seeded by rank, nn.Linear-init weights seed 0",
-            "config": {"workload": WORKLOAD, "model": "MLP 4096-16384-4096 gelu, MSE loss, SGD lr 1e-3",
-                       "global_batch": samples, "per_rank_batch": PER_RANK_BATCH, "seq_len": None,
-                       "parallelism": f"dp{world}",
-                       "l2": "inputs larger than L2 (per-step working set ~1.9 GB > 126 MB)"},
+            "config": workload_config(world),
             "steps_per_s": round(1000.0 / ms, 2),
             "step_tflops": round(model.flops_per_step() / (ms * 1e-3) / 1e12, 1),
             "train_loss": loss_value,
             "roofline": {"bound": "tensor", "kernel": "gemm_tc2_kernel (tcgen05 cta_group::2, bf16 -> fp32)",
-                         "achieved": round(achieved, 1), "peak": bf16_sustained, "unit": "TFLOP/s",
-                         "frac": round(achieved / bf16_sustained, 3), "traffic": traffic,
-                         "peak_kind": f"{peak_kind} sustained bf16 (kernel timed inside a long step)",
+                         "achieved": round(achieved, 1), "peak": bf16_peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / bf16_peak, 3), "traffic": traffic,
+                         "peak_kind": f"{peak_kind} burst bf16 (the timed region lasts well under a second)",
+                         "frac_of_sustained": round(achieved / bf16_sustained, 3),
                          "per_launch_flops": gemm_flops, "avg_launch_ms": round(gemm_avg_ms, 4),
                          "launches_timed": len(gemm_ms),
-                         "per_gemm_ms": {k: round(v, 4) for k, v in zip(
-                             ("h=xW1^T", "out=aW2^T", "dW2=dout^T a", "da=dout W2", "dW1=dh^T x"), per_gemm)}},
+                         "per_gemm_ms": {k: round(v, 4) for k, v in zip(GEMM_NAMES, per_gemm)},
+                         "traffic_by_gemm": traffic_by_gemm,
+                         "algorithmic_bytes_by_gemm": GEMM_ALGORITHMIC_BYTES},
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 4, "ms_per_step": round(e2e_ms, 4),
                     "path": "pinned host batch -> tp_b200_memcpy (copy stream, next batch prefetched) "
                             "-> step -> loss -> tp_b200_memcpy into that step's pinned host slot "
-                            "(not waited on per step; all slots checked after the timed region)"},
+                            "(not waited on per step; all slots checked after the timed region)",
+                    "h2d_only_ms_per_step": round(h2d_ms, 4),
+                    "h2d_ceiling_gb_s": round(h2d * world / (h2d_ms * 1e-3) / 1e9, 1),
+                    "ceiling_note": "the same per-step host->device copies with no compute, on every rank at "
+                                    "once (max over ranks): aggregate GB/s; the e2e step cannot be shorter "
+                                    "than h2d_only_ms_per_step"},
+            "dp_params_identical": params_identical,
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
         }
@@ -607,10 +736,11 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                 line["gemm_set"] = gemm_set(ops, bf16_peak)
                 line["quick_start"] = quick_start(ops)
             line["extras_clocks"] = extra_clocks.summary()
-        cpu_value, threads, _ = cpu_mlp_throughput(2, 1, 16)
+        cpu_value, threads, _, gflops = cpu_mlp_throughput(2, 1)
         line["cpu_baseline"] = {"value": round(cpu_value, 2), "unit": UNIT, "cores": threads, "kind": "port",
-                                "sample": "16 rows per step of the 8192-row batch, full 134M-parameter weights, "
-                                          "2 timed steps after 1 warm-up (oracle/mlp.c, all host threads)"}
+                                "gflop_s": round(gflops, 1),
+                                "sample": f"the full {PER_RANK_BATCH}-row step, 2 timed steps after 1 warm-up "
+                                          "(oracle/mlp.c's blocked fp32 products, every host core)"}
         line["peaks"] = {"hbm_gbs": hbm_peak, "bf16_tflops": bf16_peak, "bf16_tflops_sustained": bf16_sustained,
                          "kind": peak_kind}
     if rank == 0:
@@ -661,6 +791,14 @@ def run_only(args) -> None:
     elif name == "softmax_bf16":
         a = rnd(32768, 4096)
         fn = lambda: ops.softmax(a, -1)
+    elif name == "mlp_step":       # one full-size training step per launch of fn (five products)
+        from tensorplay_mlu_b200.train import DataParallelMLP, MLPConfig, init_params_host, make_batch_host
+
+        cfg = MLPConfig(d_in=D_IN, d_hidden=D_HIDDEN, batch=PER_RANK_BATCH)
+        model = DataParallelMLP(cfg, device=0, host_params=init_params_host(cfg, seed=0))
+        xh, th = make_batch_host(cfg, seed=0)
+        x, t = ops.to_device(xh), ops.to_device(th)
+        fn = lambda: model.step(x, t)
     elif name == "add_row_f32":
         a, b = rnd(8192, 8192, dt=torch.float32), rnd(8192, dt=torch.float32)
         fn = lambda: ops.add_Tensor(a, b)

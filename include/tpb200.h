@@ -323,11 +323,16 @@ int tp_b200_reduce(int op, const tpb_tensor* out, const tpb_tensor* x, uint32_t 
  * partial results go to one static 8 MiB device array per GPU (held by every
  * GPU that loads the library until the process exits).  A reduction whose
  * partial results would exceed 8 MiB, whose input layout would need a
- * gathered copy, or whose result dtype is neither the input's nor the
- * accumulator's is rejected with an error (use tp_b200_reduce).  The first
- * call on a device looks up the array's device address (cudaGetSymbolAddress
- * with that device current); make that first call before any stream capture.
- * All calls share the array, so calls whose work overlaps on the GPU race. */
+ * gathered copy, whose result dtype is neither the input's nor the
+ * accumulator's, or which reduces columns under 65536 or more outer rows, is
+ * rejected with an error (use tp_b200_reduce).  The first call on a device
+ * is its one-time set-up: with that device current it looks up the array's
+ * device address (cudaGetSymbolAddress) and loads every reduction kernel the
+ * entry point can launch.  Under CUDA's lazy module loading that set-up is
+ * where the array and the kernels' code take their device memory, so make
+ * one call on each device before its memory is reserved by a pool, and
+ * before any stream capture; no later call on that device allocates.  All
+ * calls share the array, so calls whose work overlaps on the GPU race. */
 int tp_b200_reduce_noalloc(int op, const tpb_tensor* out, const tpb_tensor* x, uint32_t dim_mask,
                            void* stream);
 /* ReduceKernels.cpp:146-199 softmax_forward over dimension `dim`

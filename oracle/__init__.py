@@ -103,6 +103,9 @@ def lib() -> ctypes.CDLL:
                              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float,
                              ctypes.POINTER(ctypes.c_float)],
             "orc_num_threads": [],
+            "orc_set_num_threads": [I],
+            "orc_gemm_blocked": [I64, I64, I64, ctypes.c_void_p, I64, I64, ctypes.c_void_p, I64, I64,
+                                 ctypes.c_void_p],
         }
         for name, args in sig.items():
             fn = getattr(handle, name)
@@ -223,6 +226,21 @@ def mlp_step(x, t, w1, b1, w2, b2, lr: float) -> float:
 
 def num_threads() -> int:
     return lib().orc_num_threads()
+
+
+def set_num_threads(n: int) -> None:
+    """OpenMP threads of the oracle's parallel loops (torchrun exports
+    OMP_NUM_THREADS=1, so the CPU baseline sets its count explicitly)."""
+    lib().orc_set_num_threads(int(n))
+
+
+def gemm_blocked(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """fp32 a @ b through mlp.c's blocked product (any strides)."""
+    assert a.dtype == b.dtype == torch.float32 and a.dim() == b.dim() == 2
+    out = torch.empty(a.shape[0], b.shape[1], dtype=torch.float32)
+    _ok(lib().orc_gemm_blocked(a.shape[0], b.shape[1], a.shape[1], a.data_ptr(), a.stride(0), a.stride(1),
+                               b.data_ptr(), b.stride(0), b.stride(1), out.data_ptr()), "gemm_blocked")
+    return out
 
 
 # ---------------------------------------------------------------------- NN

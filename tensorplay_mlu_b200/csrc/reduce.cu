@@ -1055,27 +1055,36 @@ constexpr bool ring_by_default() { return false; }
 // when none may be used: streams that are being captured into a graph (a
 // replay could run beside the stream's own launches), the per-thread default
 // stream (one handle, many streams) and more streams than slots.
-unsigned* reduce_ticket(int dev, cudaStream_t stream) {
-    if (stream == cudaStreamPerThread || dev < 0 || dev >= 64) return nullptr;
-    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-    TPB_CUDA(cudaStreamIsCapturing(stream, &cap));
-    if (cap != cudaStreamCaptureStatusNone) return nullptr;
-    static std::mutex lock;
+std::mutex g_ticket_lock;
+
+// Device address of the ticket array on `dev` (the caller has made `dev`
+// current), looked up once per device.
+unsigned* ticket_base(int dev) {
     static unsigned* base[64] = {};
-    static std::map<std::pair<int, cudaStream_t>, int> slots;
-    static int used[64] = {};
-    std::lock_guard<std::mutex> g(lock);
+    std::lock_guard<std::mutex> g(g_ticket_lock);
     if (base[dev] == nullptr) {
         void* p = nullptr;
         TPB_CUDA(cudaGetSymbolAddress(&p, g_reduce_tickets));
         base[dev] = static_cast<unsigned*>(p);
     }
+    return base[dev];
+}
+
+unsigned* reduce_ticket(int dev, cudaStream_t stream) {
+    if (stream == cudaStreamPerThread || dev < 0 || dev >= 64) return nullptr;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    TPB_CUDA(cudaStreamIsCapturing(stream, &cap));
+    if (cap != cudaStreamCaptureStatusNone) return nullptr;
+    unsigned* base = ticket_base(dev);
+    static std::map<std::pair<int, cudaStream_t>, int> slots;
+    static int used[64] = {};
+    std::lock_guard<std::mutex> g(g_ticket_lock);
     auto it = slots.find({dev, stream});
     if (it == slots.end()) {
         if (used[dev] >= kTicketSlots) return nullptr;
         it = slots.emplace(std::make_pair(dev, stream), used[dev]++).first;
     }
-    return base[dev] + it->second;
+    return base + it->second;
 }
 
 // Row-kernel plan.  Three kernels:
@@ -1454,9 +1463,48 @@ namespace {
 std::mutex g_noalloc_lock;
 void* g_noalloc_ptr[64] = {};
 
+// Every kernel the allocation-free path can launch for input type T, result
+// type To and operation OP, loaded now: under lazy module loading (the CUDA
+// 12 default) a kernel's code is otherwise loaded, and device memory taken
+// for it, at its first launch.  The occupancy queries the plans make are
+// answered and cached here too.
+template <typename T, typename To, int OP>
+void preload_kernels(int dev, int sms) {
+    using A = typename Acc<T>::type;
+    constexpr int V = VecWidth<T>::value;
+    cudaFuncAttributes fa;
+    TPB_CUDA(cudaFuncGetAttributes(&fa, reduce_rows<T, To, OP>));
+    TPB_CUDA(cudaFuncGetAttributes(&fa, reduce_rows_warp<T, To, OP>));
+    TPB_CUDA(cudaFuncGetAttributes(&fa, reduce_rows_ring<T, To, OP>));
+    TPB_CUDA(cudaFuncGetAttributes(&fa, reduce_row_partials<A, To, OP>));
+    TPB_CUDA(cudaFuncGetAttributes(&fa, reduce_cols<T, To, OP, V, 1>));
+    TPB_CUDA(cudaFuncGetAttributes(&fa, reduce_cols<T, To, OP, 1, 1>));
+    TPB_CUDA(cudaFuncGetAttributes(&fa, reduce_cols<T, To, OP, V, kColLanes>));
+    TPB_CUDA(cudaFuncGetAttributes(&fa, reduce_cols<T, To, OP, 1, kColLanes>));
+    TPB_CUDA(cudaFuncGetAttributes(&fa, reduce_col_partials<A, To, OP>));
+    (void)rows_capacity<T, To, OP>(dev, sms);
+    (void)plan_cols<T, To, OP>(1, 1, 1, false, dev, sms);
+}
+
+template <typename T>
+void preload_type(int dev, int sms) {
+    using A = typename Acc<T>::type;
+    preload_kernels<T, T, TPB_SUM>(dev, sms);
+    preload_kernels<T, T, TPB_MEAN>(dev, sms);
+    preload_kernels<T, T, TPB_AMAX>(dev, sms);
+    preload_kernels<T, T, TPB_AMIN>(dev, sms);
+    if constexpr (!std::is_same<T, A>::value) {
+        preload_kernels<T, A, TPB_SUM>(dev, sms);
+        preload_kernels<T, A, TPB_MEAN>(dev, sms);
+    }
+}
+
 // Device address of the array on `dev` (the caller has made `dev` current).
 // In host code the array's name is only a host-side handle, so the address is
-// looked up once per device and cached.
+// looked up once per device and cached.  That first lookup is the entry
+// point's set-up on the device: it loads this file's module (committing the
+// array and the completion tickets) and every kernel the entry point can
+// launch, so that no later call on the device takes device memory.
 void* noalloc_scratch(int dev) {
     TPB_CHECK(dev >= 0 && dev < 64, "invalid device index %d", dev);
     std::lock_guard<std::mutex> lock(g_noalloc_lock);
@@ -1464,6 +1512,18 @@ void* noalloc_scratch(int dev) {
         void* p = nullptr;
         TPB_CUDA(cudaGetSymbolAddress(&p, g_reduce_noalloc_scratch));
         TPB_CHECK(p != nullptr, "reduce_noalloc: no device address for the static scratch");
+        (void)ticket_base(dev);
+        const int sms = num_sms(dev);
+        preload_type<uint8_t>(dev, sms);
+        preload_type<int8_t>(dev, sms);
+        preload_type<int16_t>(dev, sms);
+        preload_type<int32_t>(dev, sms);
+        preload_type<int64_t>(dev, sms);
+        preload_type<__half>(dev, sms);
+        preload_type<float>(dev, sms);
+        preload_type<__nv_bfloat16>(dev, sms);
+        preload_type<double>(dev, sms);
+        preload_type<bool>(dev, sms);
         g_noalloc_ptr[dev] = p;
     }
     return g_noalloc_ptr[dev];
@@ -1494,10 +1554,10 @@ void reduce_launch_noalloc(const tpb_tensor& out, const tpb_tensor& xin, uint32_
     }
     const int64_t rows = kept.numel();
     const int64_t R = red.numel();
-    if (R == 1) {
-        copy_impl(out, xin, stream, dev);
-        return;
-    }
+    // R == 1 (nothing to reduce) runs through the row kernels below like any
+    // other reduction (one element per row; exact for every op and result
+    // type), not through a copy, whose kernels live in another module that
+    // the set-up does not load.
     kept.coalesce();
     red.coalesce();
     To* o = static_cast<To*>(out.data);

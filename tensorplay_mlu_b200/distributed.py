@@ -87,13 +87,27 @@ def _flat(t: torch.Tensor) -> torch.Tensor:
 
 
 class _Work:
-    """Handle for collectives enqueued on a stream that has not drained yet."""
+    """Handle for collectives enqueued on a stream that has not drained yet.
 
-    def __init__(self, device: int, stream: torch.cuda.Stream, done=None) -> None:
+    ``wait()`` without a timeout makes the caller's current stream wait for
+    the collective (no host block), as a CUDA process group's work does.
+    ``wait(timeout)`` also bounds it on the host: it polls the collective's
+    completion and the communicator's asynchronous error until the deadline,
+    and a collective that has not finished by then aborts the communicator
+    and raises ``TimeoutError`` -- a stuck peer becomes an error instead of
+    a hang (tensorplay-mlu's wait ignores its timeout,
+    tensorplay_mlu/distributed.py:113-118)."""
+
+    POLL_S = 0.001
+
+    def __init__(self, device: int, stream, done=None, group=None, event=None) -> None:
         self._device = device
-        self._event = torch.cuda.Event()
-        self._event.record(stream)
+        if event is None:
+            event = torch.cuda.Event()
+            event.record(stream)
+        self._event = event
         self._done = done
+        self._group = group
         self._finished = False
 
     def _finish(self) -> None:
@@ -111,8 +125,20 @@ class _Work:
         return False
 
     def wait(self, timeout=None) -> bool:
-        # The caller's current stream waits for the collective (no host block),
-        # as a CUDA process group's work does.
+        seconds = _seconds(timeout)
+        if seconds is not None and seconds > 0:
+            deadline = time.monotonic() + seconds
+            while not self._event.query():
+                if self._group is not None:
+                    self._group.check()  # raises on an asynchronous NCCL error
+                if time.monotonic() > deadline:
+                    if self._group is not None:
+                        self._group.abort()
+                    raise TimeoutError(f"collective did not complete within {seconds} s; "
+                                       "the communicator was aborted")
+                time.sleep(self.POLL_S)
+            self._finish()
+            return True
         torch.cuda.current_stream(self._device).wait_event(self._event)
         self._finish()
         return True
@@ -124,6 +150,15 @@ class _Work:
     def abort(self) -> None:
         raise RuntimeError("abort is unavailable for an individual NCCL work item; "
                            "abort the process group's communicator instead")
+
+
+def _seconds(timeout) -> Optional[float]:
+    """A work timeout in seconds: a number of seconds or a timedelta."""
+    if timeout is None:
+        return None
+    if hasattr(timeout, "total_seconds"):
+        return float(timeout.total_seconds())
+    return float(timeout)
 
 
 class ProcessGroupB200:
@@ -196,7 +231,7 @@ class ProcessGroupB200:
         return N.lib(), stream
 
     def _work(self, stream) -> _Work:
-        return _Work(self._device, stream)
+        return _Work(self._device, stream, group=self)
 
     def _reduction(self, op: int):
         try:
@@ -331,6 +366,140 @@ class ProcessGroupB200:
             _check(lib.tp_b200_nccl_reduce_scatter(_ptr(input_tensor), _ptr(output), count,
                                                    _dtype_code(output), code, self._device, self._comm))
             self._scale(output, scale)
+        return self._work(stream)
+
+    def reduce_scatter_single_coalesced(self, outputs: List[torch.Tensor], inputs: List[torch.Tensor],
+                                        op: int = ReduceOp.SUM, timeout_ms: int = 0):
+        """One reduce-scatter per (output, input) pair, issued as one NCCL
+        group (tensorplay_mlu/distributed.py:391-407)."""
+        lib, stream = self._enter()
+        code, scale = self._reduction(op)
+        _check(lib.tp_b200_nccl_group_start())
+        for output, input_tensor in zip(outputs, inputs):
+            count = int(output.numel())
+            if count:
+                _check(lib.tp_b200_nccl_reduce_scatter(_ptr(input_tensor), _ptr(output), count,
+                                                       _dtype_code(output), code, self._device, self._comm))
+        _check(lib.tp_b200_nccl_group_end())
+        for output in outputs:
+            self._scale(output, scale)
+        return self._work(stream)
+
+    def all_gather_single_coalesced(self, outputs: List[torch.Tensor], inputs: List[torch.Tensor],
+                                    timeout_ms: int = 0):
+        """One all-gather per (output, input) pair, issued as one NCCL group
+        (tensorplay_mlu/distributed.py:328-340)."""
+        lib, stream = self._enter()
+        _check(lib.tp_b200_nccl_group_start())
+        for output, input_tensor in zip(outputs, inputs):
+            count = int(input_tensor.numel())
+            if count:
+                _check(lib.tp_b200_nccl_all_gather(_ptr(input_tensor), _ptr(output), count,
+                                                   _dtype_code(input_tensor), self._device, self._comm))
+        _check(lib.tp_b200_nccl_group_end())
+        return self._work(stream)
+
+    def allgather_coalesced(self, output_lists, input_tensors: List[torch.Tensor], timeout_ms: int = 0):
+        """All-gather of each input into the per-rank lists
+        (``output_lists[rank][index]``), issued as one NCCL group
+        (tensorplay_mlu/distributed.py:342-363); each tensor's rank chunks
+        go through one dense buffer, copied out once the group has run."""
+        lib, stream = self._enter()
+        staged = []
+        _check(lib.tp_b200_nccl_group_start())
+        for index, tensor in enumerate(input_tensors):
+            count = int(tensor.numel())
+            if not count:
+                continue
+            chunks = [rank_outputs[index] for rank_outputs in output_lists]
+            flat = torch.empty((count * self._size,), dtype=tensor.dtype, device=tensor.device)
+            _check(lib.tp_b200_nccl_all_gather(_ptr(_flat(tensor)), _ptr(flat), count, _dtype_code(tensor),
+                                               self._device, self._comm))
+            staged.append((flat, chunks))
+        _check(lib.tp_b200_nccl_group_end())
+        for flat, chunks in staged:
+            self._scatter_from(flat, chunks)
+        return self._work(stream)
+
+    def gather(self, output_lists, input_tensors: List[torch.Tensor], root: int = 0, timeout_ms: int = 0):
+        """Every rank's ``input_tensors[0]`` into ``output_lists[0][rank]`` on
+        ``root``, over point-to-point sends (tensorplay_mlu/distributed.py:410-431)."""
+        from . import ops
+
+        lib, stream = self._enter()
+        tensor = input_tensors[0]
+        count = int(tensor.numel())
+        dtype = _dtype_code(tensor)
+        staged = []
+        _check(lib.tp_b200_nccl_group_start())
+        if self._rank == root:
+            for peer in range(self._size):
+                target = output_lists[0][peer]
+                if peer == root:
+                    if count:
+                        ops.copy_(target, _flat(tensor).reshape(target.shape))
+                elif count:
+                    buf = target if target.is_contiguous() else torch.empty_like(target)
+                    _check(lib.tp_b200_nccl_recv(_ptr(buf), count, dtype, peer, self._device, self._comm))
+                    if buf is not target:
+                        staged.append((target, buf))
+        elif count:
+            _check(lib.tp_b200_nccl_send(_ptr(_flat(tensor)), count, dtype, root, self._device, self._comm))
+        _check(lib.tp_b200_nccl_group_end())
+        for target, buf in staged:
+            ops.copy_(target, buf)
+        return self._work(stream)
+
+    def gather_single(self, output: torch.Tensor, input_tensor: torch.Tensor, root: int = 0,
+                      timeout_ms: int = 0):
+        """Rank r's input into elements [r * n, (r + 1) * n) of ``output`` on
+        ``root`` (tensorplay_mlu/distributed.py:433-452)."""
+        from . import ops
+
+        lib, stream = self._enter()
+        count = int(input_tensor.numel())
+        dtype = _dtype_code(input_tensor)
+        if self._rank == root:
+            flat_out = _flat(output)
+            _check(lib.tp_b200_nccl_group_start())
+            for peer in range(self._size):
+                if peer != root and count:
+                    _check(lib.tp_b200_nccl_recv(_ptr(flat_out.narrow(0, peer * count, count)), count, dtype,
+                                                 peer, self._device, self._comm))
+            _check(lib.tp_b200_nccl_group_end())
+            if count:
+                ops.copy_(flat_out.narrow(0, root * count, count), _flat(input_tensor))
+            self._write_back(output, flat_out)
+        elif count:
+            _check(lib.tp_b200_nccl_group_start())
+            _check(lib.tp_b200_nccl_send(_ptr(_flat(input_tensor)), count, dtype, root, self._device,
+                                         self._comm))
+            _check(lib.tp_b200_nccl_group_end())
+        return self._work(stream)
+
+    def scatter(self, recv_tensors: List[torch.Tensor], input_lists, root: int = 0, timeout_ms: int = 0):
+        """``input_lists[0][r]`` on ``root`` into rank r's ``recv_tensors[0]``
+        (tensorplay_mlu/distributed.py:454-470)."""
+        from . import ops
+
+        lib, stream = self._enter()
+        output = recv_tensors[0]
+        count = int(output.numel())
+        dtype = _dtype_code(output)
+        buf = output if output.is_contiguous() else torch.empty_like(output)
+        _check(lib.tp_b200_nccl_group_start())
+        if self._rank == root:
+            for peer in range(self._size):
+                if peer != root and count:
+                    _check(lib.tp_b200_nccl_send(_ptr(_flat(input_lists[0][peer])), count, dtype, peer,
+                                                 self._device, self._comm))
+        elif count:
+            _check(lib.tp_b200_nccl_recv(_ptr(buf), count, dtype, root, self._device, self._comm))
+        _check(lib.tp_b200_nccl_group_end())
+        if self._rank == root and count:
+            ops.copy_(output, _flat(input_lists[0][root]).reshape(output.shape))
+        elif buf is not output:
+            ops.copy_(output, buf)
         return self._work(stream)
 
     def all_to_all_single(self, output: torch.Tensor, input_tensor: torch.Tensor,

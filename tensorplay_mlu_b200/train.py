@@ -107,6 +107,8 @@ class DataParallelMLP:
         # When a list, every GEMM of the step appends a (start, end) pair of
         # CUDA events recorded around its launch on the current stream.
         self.gemm_events: Optional[list] = None
+        # When a dict, the step stores its intermediates in it (for checks).
+        self.trace: Optional[dict] = None
 
     def _timed(self, fn, *args):
         if self.gemm_events is None:
@@ -173,6 +175,8 @@ class DataParallelMLP:
         else:
             d_a = self._timed(ops.mm, d_out, self.w2)
         d_h = ops.gelu_backward(d_a, h)
+        if self.trace is not None:
+            self.trace.update(x=x, t=target, h=h, a=a, out=out, d_out=d_out, d_a=d_a, d_h=d_h, loss=loss)
         if self.comm_stream is None:
             self._timed(self._mm_into, self.dw1, d_h.t(), x)
             self._colsum_into(self.db1, d_h)

@@ -50,6 +50,32 @@ def assert_close(got: torch.Tensor, want: torch.Tensor, dtype=None, scale: float
     assert err <= TOL[dtype] * ref, f"max error {err} > {TOL[dtype] * ref} ({dtype})"
 
 
+def assert_close_terms(got: torch.Tensor, want: torch.Tensor, terms, dtype=None) -> None:
+    """The bound for results that are sums -- reductions, products, scans,
+    scatter-adds: max|got - want| <= TOL * max(max(terms), 1), where `terms`
+    is the magnitude of what was summed into each result (sum |x_i| for a
+    sum, sum |a_k b_k| for a product; a tensor shaped like `want`, or a
+    number).  Rounding errors of a sum scale with its terms, not with its
+    value, which cancellation can make arbitrarily small; so this is the same
+    relative tolerance (fp32 1e-5, bf16 1e-2) taken against the terms,
+    with no extra factor."""
+    dtype = dtype or want.dtype
+    got = got.detach().cpu()
+    want = want.detach().cpu()
+    assert tuple(got.shape) == tuple(want.shape), (tuple(got.shape), tuple(want.shape))
+    if got.numel() == 0:
+        return
+    g, w = got.double(), want.double()
+    assert torch.equal(torch.isnan(g), torch.isnan(w)), "NaN positions differ"
+    nan = torch.isnan(g)
+    g = torch.where(nan, torch.zeros_like(g), g)
+    w = torch.where(nan, torch.zeros_like(w), w)
+    err = (g - w).abs().max().item()
+    t = terms.detach().double().abs().max().item() if isinstance(terms, torch.Tensor) else abs(float(terms))
+    ref = max(t, w.abs().max().item(), 1.0)
+    assert err <= TOL[dtype] * ref, f"max error {err} > {TOL[dtype] * ref} ({dtype}, terms {t})"
+
+
 def assert_equal(got: torch.Tensor, want: torch.Tensor) -> None:
     got, want = got.detach().cpu(), want.detach().cpu()
     assert got.dtype == want.dtype, (got.dtype, want.dtype)

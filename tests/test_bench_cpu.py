@@ -22,14 +22,21 @@ def test_op_sweep_reports_the_median_pass_and_its_spread(monkeypatch):
 
 def test_clock_summary_lists_active_throttle_reasons():
     s = bench.ClockSampler(0)
-    s.lines = [
+    s.source = "nvidia-smi"
+    s.add_smi_lines([
         "0, 1965, 1965, 700.0, 0x0, Not Active, Not Active, Not Active, Not Active",
         "0, 1410, 1965, 1000.0, 0x4, Not Active, Not Active, Not Active, Active",
         "0, 1380, 1965, 1000.0, 0x4, Not Active, Not Active, Not Active, Active",
-    ]
+        "garbage",
+    ])
     out = s.summary()
-    assert out["sm_mhz"] == 1410 and out["sm_max_mhz"] == 1965
+    assert out["sm_mhz"] == 1410 and out["sm_max_mhz"] == 1965 and out["sm_mhz_min"] == 1380
     assert out["reasons"] == ["sw_power_cap"] and out["samples"] == 3
-    empty = bench.ClockSampler(0)
-    empty.lines = []
-    assert empty.summary()["reasons"] == ["unsampled"]
+    assert bench.ClockSampler(0).summary()["reasons"] == ["unsampled"]
+
+
+def test_clock_summary_from_nvml_flags():
+    s = bench.ClockSampler(0)
+    s.source = "nvml"
+    s.rows = [(1965.0, 1965.0, [False, False, False, False]), (1900.0, 1965.0, [True, False, False, False])]
+    assert s.summary()["reasons"] == ["hw_slowdown"]

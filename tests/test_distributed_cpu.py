@@ -129,3 +129,66 @@ def test_native_errors_surface_as_exceptions():
             pg.ensure()
     finally:
         _native.lib = real
+
+
+class _NeverDone:
+    """A collective's completion event that never fires (a stuck peer)."""
+
+    def query(self):
+        return False
+
+
+class _Group:
+    def __init__(self, error_after=None):
+        self.aborted = False
+        self.checks = 0
+        self.error_after = error_after
+
+    def check(self):
+        self.checks += 1
+        if self.error_after is not None and self.checks >= self.error_after:
+            raise RuntimeError("NCCL asynchronous error: remote process exited")
+
+    def abort(self):
+        self.aborted = True
+
+
+def test_work_wait_with_a_timeout_aborts_a_stuck_collective():
+    import datetime
+
+    from tensorplay_mlu_b200.distributed import _Work
+
+    group = _Group()
+    work = _Work(0, None, group=group, event=_NeverDone())
+    start = time.monotonic()
+    with pytest.raises(TimeoutError):
+        work.wait(timeout=datetime.timedelta(milliseconds=200))
+    assert 0.2 <= time.monotonic() - start < 5.0
+    assert group.aborted and group.checks > 0
+    assert not work.is_completed()
+
+
+def test_work_wait_surfaces_an_asynchronous_communicator_error():
+    from tensorplay_mlu_b200.distributed import _Work
+
+    group = _Group(error_after=3)
+    work = _Work(0, None, group=group, event=_NeverDone())
+    with pytest.raises(RuntimeError, match="asynchronous error"):
+        work.wait(timeout=30.0)
+    assert not group.aborted
+
+
+def test_work_wait_returns_once_the_collective_completes():
+    from tensorplay_mlu_b200.distributed import _Work
+
+    class DoneAfter:
+        def __init__(self, n):
+            self.n = n
+
+        def query(self):
+            self.n -= 1
+            return self.n <= 0
+
+    finished = []
+    work = _Work(0, None, done=lambda: finished.append(1), group=_Group(), event=DoneAfter(5))
+    assert work.wait(timeout=5.0) and work.is_completed() and finished == [1]

@@ -125,3 +125,33 @@ def test_large_bf16_all_reduce_is_identity_on_one_rank(backend):
         work.synchronize()
         assert work.is_completed()
         assert torch.equal(backend.ops.to_host(x), h)
+
+
+def test_gather_scatter_and_coalesced_forms(backend):
+    # tensorplay_mlu/distributed.py:328-470: on one rank every form is the identity.
+    from tensorplay_mlu_b200.distributed import ReduceOp
+
+    with single_rank(backend) as pg:
+        x = t(backend, [1.0, 2.0, 3.0])
+        out = [backend.ops.zero_(torch.empty(3, device="cuda"))]
+        pg.gather([out], [x], 0).wait()
+        assert host(backend, out[0]) == [1.0, 2.0, 3.0]
+        flat = backend.ops.zero_(torch.empty(3, device="cuda"))
+        pg.gather_single(flat, x, 0).wait()
+        assert host(backend, flat) == [1.0, 2.0, 3.0]
+        recv = backend.ops.zero_(torch.empty(3, device="cuda"))
+        pg.scatter([recv], [[x]], 0).wait()
+        assert host(backend, recv) == [1.0, 2.0, 3.0]
+        ys = [t(backend, [5.0]), t(backend, [6.0, 7.0], torch.bfloat16)]
+        outs = [[backend.ops.zero_(torch.empty(1, device="cuda")),
+                 backend.ops.zero_(torch.empty(2, dtype=torch.bfloat16, device="cuda"))]]
+        pg.allgather_coalesced(outs, ys).wait()
+        assert host(backend, outs[0][0]) == [5.0] and host(backend, outs[0][1]) == [6.0, 7.0]
+        singles = [backend.ops.zero_(torch.empty(1, device="cuda")),
+                   backend.ops.zero_(torch.empty(2, dtype=torch.bfloat16, device="cuda"))]
+        pg.all_gather_single_coalesced(singles, ys).wait()
+        assert host(backend, singles[0]) == [5.0] and host(backend, singles[1]) == [6.0, 7.0]
+        reds = [backend.ops.zero_(torch.empty(1, device="cuda")),
+                backend.ops.zero_(torch.empty(2, dtype=torch.bfloat16, device="cuda"))]
+        pg.reduce_scatter_single_coalesced(reds, ys, ReduceOp.AVG).wait(timeout=30)
+        assert host(backend, reds[0]) == [5.0] and host(backend, reds[1]) == [6.0, 7.0]
