@@ -477,10 +477,16 @@ def gemm_set(ops, bf16_peak: float):
     return res
 
 
+# NVLink 5 per GPU and direction (18 links through NVSwitch), the roofline of
+# the collective sweep's bus bandwidth.
+NVLINK_GBS = 900.0
+
+
 def collective_sweep(pg, host, ops, world: int, max_bytes: int = 1 << 30):
     """BASELINE config 5b: NCCL collectives through the nccl_b200 process group,
     bus bandwidth by the nccl-tests convention (all_reduce 2(n-1)/n, others
-    (n-1)/n), time = max over ranks of CUDA-event time."""
+    (n-1)/n), time = max over ranks of CUDA-event time; nvlink_frac = bus
+    bandwidth / 900 GB/s (NVLink 5 per GPU and direction)."""
     res = {}
     sizes = []
     s = 4096
@@ -516,7 +522,8 @@ def collective_sweep(pg, host, ops, world: int, max_bytes: int = 1 << 30):
                 algbw = n * es / (ms * 1e-3) / 1e9
                 res.setdefault(f"{name}_{tag}", []).append(
                     {"bytes": n * es, "ms": round(ms, 4), "algbw_gb_s": round(algbw, 1),
-                     "busbw_gb_s": round(algbw * factor, 1)})
+                     "busbw_gb_s": round(algbw * factor, 1),
+                     "nvlink_frac": round(algbw * factor / NVLINK_GBS, 3)})
             del buf, out, part
     return res
 
@@ -568,7 +575,12 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     # TPB200_DW1_SLICES overrides how many slices the last gradient bucket is
     # exchanged in (A/B measurements; the default is MLPConfig's).
     slices = int(os.environ.get("TPB200_DW1_SLICES", MLPConfig.dw1_slices))
-    cfg = MLPConfig(d_in=D_IN, d_hidden=D_HIDDEN, batch=PER_RANK_BATCH, dw1_slices=slices)
+    # Bucket B's update deferred into the next step (TPB200_OVERLAP_NEXT=0
+    # applies it at the end of each step instead, for A/B measurements);
+    # flush() inside each timed region completes the last step's update.
+    overlap = os.environ.get("TPB200_OVERLAP_NEXT", "1") != "0"
+    cfg = MLPConfig(d_in=D_IN, d_hidden=D_HIDDEN, batch=PER_RANK_BATCH, dw1_slices=slices,
+                    overlap_next_step=overlap)
     model = DataParallelMLP(cfg, device=local, pg=pg, host_params=init_params_host(cfg, seed=0))
     xh, th = make_batch_host(cfg, seed=rank)
     x, t = ops.to_device(xh), ops.to_device(th)
@@ -576,6 +588,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     # ---- device-resident timing (the headline value)
     for _ in range(args.warmup):
         model.step(x, t)
+    model.flush()
     torch.cuda.synchronize()
     host.barrier()
     launches0 = N.lib().tp_b200_launch_count()
@@ -587,6 +600,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         start.record()
         for _ in range(args.steps):
             loss = model.step(x, t)
+        model.flush()
         end.record()
         end.synchronize()
         host.barrier()
@@ -638,12 +652,14 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                                            N.stream_of(local), 0), "d2h")
 
     e2e_steps(max(1, args.warmup // 2))
+    model.flush()
     torch.cuda.synchronize()
     host.barrier()
     t0 = time.perf_counter()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     e2e_steps(args.steps)
+    model.flush()
     e1.record()
     e1.synchronize()
     e2e_ms = host.max(e0.elapsed_time(e1) / args.steps)
@@ -711,6 +727,8 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                                     "once (max over ranks): aggregate GB/s; the e2e step cannot be shorter "
                                     "than h2d_only_ms_per_step"},
             "dp_params_identical": params_identical,
+            "dp_schedule": {"dw1_slices": cfg.dw1_slices, "overlap_next_step": cfg.overlap_next_step,
+                            "gemm_sm_reserve": cfg.comm_sms} if world > 1 else None,
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
         }
@@ -721,6 +739,10 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             sweep = collective_sweep(pg, host, ops, world)
             if rank == 0:
                 line["collectives"] = sweep
+                # The largest size of each row, last in the line.
+                line["collectives_summary"] = {
+                    k: {"bytes": v[-1]["bytes"], "busbw_gb_s": v[-1]["busbw_gb_s"], "nvlink_frac": v[-1]["nvlink_frac"]}
+                    for k, v in sweep.items()}
         torch.cuda.synchronize()
         host.barrier()
         pg.destroy()
@@ -791,6 +813,27 @@ def run_only(args) -> None:
     elif name == "softmax_bf16":
         a = rnd(32768, 4096)
         fn = lambda: ops.softmax(a, -1)
+    elif name in ("gemm_gelu", "gemm_gelu_bwd", "gemm_linear_h"):
+        # the step's first / fourth product with and without the fused epilogue
+        from tensorplay_mlu_b200 import _native as N
+
+        x, w, bias = rnd(8192, 4096), rnd(16384, 4096, scale=4096 ** -0.5), rnd(16384)
+        h, a = torch.empty(8192, 16384, dtype=torch.bfloat16, device="cuda"), torch.empty(
+            8192, 16384, dtype=torch.bfloat16, device="cuda")
+        d_out, w2 = rnd(8192, 4096, scale=1e-3), rnd(4096, 16384, scale=4096 ** -0.5)
+
+        def epi(code, out, aux, A, B, c=None):
+            N.check(N.lib().tp_b200_gemm_epilogue(code, N.describe(out), N.describe(aux), N.describe(A),
+                                                  N.describe(B), N.describe(c) if c is not None else None, 1.0,
+                                                  1.0 if c is not None else 0.0, 0, N.stream_of(out.device)),
+                    "gemm_epilogue")
+
+        if name == "gemm_gelu":
+            fn = lambda: epi(N.EPI_GELU, a, h, x, w.t(), bias)
+        elif name == "gemm_gelu_bwd":
+            fn = lambda: epi(N.EPI_GELU_BACKWARD, a, h, d_out, w2)
+        else:
+            fn = lambda: ops.linear(x, w, bias)
     elif name == "mlp_step":       # one full-size training step per launch of fn (five products)
         from tensorplay_mlu_b200.train import DataParallelMLP, MLPConfig, init_params_host, make_batch_host
 

@@ -107,6 +107,13 @@ int64_t tp_b200_launch_count(void);
  * scheduled tiles.  Process-wide per device; affects launches, not
  * kernels already queued. */
 int tp_b200_set_gemm_sm_limit(int dev, int sms);
+/* Tile order of the CTA-pair tensor-core GEMMs launched afterwards on `dev`:
+ * 0 (default) a fixed order (tile c + i * clusters to cluster c); non-zero
+ * claimed at run time, each cluster taking the next tile when it is ready,
+ * so clusters that start late (SMs held by a concurrent kernel such as a
+ * collective) take fewer tiles.  Launches captured into a graph always use
+ * the fixed order.  No reference counterpart (CNNL schedules internally). */
+int tp_b200_set_gemm_tile_order(int dev, int dynamic);
 
 /* ------------------------------------------------------------------------
  * Normalisation and loss (replaces tensorplay_mlu/csrc/NNKernels.cpp:59-161,
@@ -142,6 +149,16 @@ int tp_b200_dropout(const tpb_tensor* out, const tpb_tensor* mask, const tpb_ten
                     uint64_t seed, uint64_t offset, void* stream);
 int tp_b200_masked_scale(const tpb_tensor* dx, const tpb_tensor* dy, const tpb_tensor* mask, double scale,
                          void* stream);
+/* The mean-squared-error loss with its gradient in one pass (no single
+ * counterpart in the reference: it is the autograd sequence sub -> pow -> mean
+ * with mul for the gradient, BinaryKernels.cpp:148-248, UnaryKernels.cpp:140-186,
+ * ReduceKernels.cpp:105-111): diff = out - target; loss (one element of out's
+ * dtype) = mean(diff^2); grad (may be NULL) = diff * grad_scale.  diff,
+ * diff^2 and grad are rounded to the dtype where those operators round;
+ * the sum accumulates in fp32 (fp64 for float64) in a fixed order.
+ * Contiguous operands of one floating dtype. */
+int tp_b200_mse_loss(const tpb_tensor* loss, const tpb_tensor* grad, const tpb_tensor* out,
+                     const tpb_tensor* target, double grad_scale, void* stream);
 
 /* ------------------------------------------------------------------------
  * Indexing, scatter, scans, where (replaces tensorplay_mlu/csrc/
@@ -360,6 +377,27 @@ int tp_b200_softmax_backward(int log, const tpb_tensor* dx, const tpb_tensor* dy
  * f64 and integer types run on CUDA cores. */
 int tp_b200_gemm(const tpb_tensor* out, const tpb_tensor* a, const tpb_tensor* b,
                  const tpb_tensor* c, double alpha, double beta, int flags, void* stream);
+
+/* Epilogues that tp_b200_gemm_epilogue applies inside the product. */
+enum tpb_gemm_epilogue { TPB_EPI_GELU = 1, TPB_EPI_GELU_BACKWARD = 2 };
+
+/* A product with its activation fused into the epilogue (no single
+ * counterpart in the reference: it is the sequence linear -> gelu
+ * (BlasKernels.cpp:374-386 then UnaryKernels.cpp:52-80), or mm ->
+ * gelu_backward (BlasKernels.cpp:250-262 then UnaryKernels.cpp:222-240), in
+ * one pass over the result).  2-d operands, one floating dtype.
+ *   TPB_EPI_GELU:          aux = alpha * a @ b + beta * c (the
+ *                          pre-activation, kept for the backward pass),
+ *                          out = gelu(aux);
+ *   TPB_EPI_GELU_BACKWARD: out = gelu_backward(alpha * a @ b, aux), aux the
+ *                          activation's input; no addend.
+ * Each intermediate is rounded to the dtype exactly where the separate
+ * operators round it, so the result has the bits of the two-operator
+ * sequence.  bf16 products of at least one 256 x 256 tile run fused on the
+ * tcgen05 CTA-pair kernel; others run as the two operators. */
+int tp_b200_gemm_epilogue(int epilogue, const tpb_tensor* out, const tpb_tensor* aux,
+                          const tpb_tensor* a, const tpb_tensor* b, const tpb_tensor* c,
+                          double alpha, double beta, int flags, void* stream);
 
 /* ------------------------------------------------------------------------
  * Collectives over NCCL (replaces tensorplay_mlu/csrc/Cncl.cpp:71-387; same

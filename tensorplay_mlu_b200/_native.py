@@ -41,6 +41,7 @@ ADD, SUB, MUL, DIV, RSUB = range(5)
 (THRESHOLD_BACKWARD, SIGMOID_BACKWARD, TANH_BACKWARD, GELU_BACKWARD, GELU_TANH_BACKWARD,
  SILU_BACKWARD) = range(6)
 SUM, MEAN, AMAX, AMIN = range(4)
+EPI_GELU, EPI_GELU_BACKWARD = 1, 2  # tp_b200_gemm_epilogue
 GEMM_ALLOW_TF32 = 1
 
 
@@ -97,6 +98,7 @@ _SIGNATURES = {
     "tp_b200_take_device_error": ([_I], _I),
     "tp_b200_launch_count": ([], _I64),
     "tp_b200_set_gemm_sm_limit": ([_I, _I], _I),
+    "tp_b200_set_gemm_tile_order": ([_I, _I], _I),
     "tp_b200_capture_ready": ([], _I),
     "tp_b200_capture_stats": ([ctypes.POINTER(ctypes.c_int64)], None),
     "tp_b200_capture_begin": ([_I], _I),
@@ -124,6 +126,8 @@ _SIGNATURES = {
     "tp_b200_softmax": ([_I, _T, _T, _I, _P], _I),
     "tp_b200_softmax_backward": ([_I, _T, _T, _T, _I, _P], _I),
     "tp_b200_gemm": ([_T, _T, _T, _T, _D, _D, _I, _P], _I),
+    "tp_b200_gemm_epilogue": ([_I, _T, _T, _T, _T, _T, _D, _D, _I, _P], _I),
+    "tp_b200_mse_loss": ([_T, _T, _T, _T, _D, _P], _I),
     "tp_b200_gather": ([_T, _T, _T, _I, _P], _I),
     "tp_b200_index_select": ([_T, _T, _T, _I, _P], _I),
     "tp_b200_index_add": ([_T, _T, _T, _I, _P], _I),

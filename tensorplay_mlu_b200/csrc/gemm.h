@@ -21,6 +21,12 @@ struct GemmProblem {
     int64_t sci_b, sci_m, sci_n;
     double alpha, beta;
     int flags;
+    // Fused epilogue (tp_b200_gemm_epilogue): 0 none, 1 gelu (aux receives
+    // the pre-activation), 2 gelu_backward (aux holds the activation's
+    // input).  aux: [M x N], unit column stride, row stride saux_m.
+    int epi;
+    void* aux;
+    int64_t saux_m;
 };
 
 void gemm_simt(const GemmProblem& p, int dev, cudaStream_t stream);

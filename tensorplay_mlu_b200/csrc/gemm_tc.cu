@@ -37,6 +37,7 @@
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -46,6 +47,7 @@
 
 #include "common.h"
 #include "device.cuh"
+#include "ew_common.cuh"
 #include "gemm.h"
 #include "ptx.cuh"
 
@@ -55,7 +57,7 @@ void copy_impl(const tpb_tensor& dst, const tpb_tensor& src, cudaStream_t stream
 
 namespace {
 
-constexpr int kThreads = 320;  // warp 0 producer, warp 1 MMA, warps 2-9 epilogue
+constexpr int kTcThreads = 320;  // warp 0 producer, warp 1 MMA, warps 2-9 epilogue
 constexpr int kEpilogueWarps = 8;
 constexpr int kBM = 128;
 constexpr int kGroupM = 16;
@@ -171,8 +173,32 @@ struct TcParams {
     float alpha, beta;
     int vec_store;    // 16-byte stores allowed
     int tma_store;    // result written through the C tensor map (TMA stores)
+    const void* aux;  // kEpiGeluBackward: the activation's input h [M x N], row stride saux_m
+    int64_t saux_m;
+    // CTA-pair kernel: tiles claimed at run time from this counter word (see
+    // next_pair_tile), or in a fixed order when null.
+    unsigned long long* sched;
+    uint32_t epoch;
+    // L2 eviction priority (CTA-pair kernel): l2_operands 1 keeps A / B
+    // panels (evict_last); l2_stream 1 lets the epilogue's result stores
+    // and activation-input loads go first (evict_first).
+    int l2_operands, l2_stream;
     int* err;
 };
+
+// Epilogue forms (template argument of the CTA-pair kernel).
+//   kEpiPlain         C = alpha * acc + beta * addend
+//   kEpiGelu          v = alpha * acc + beta * addend; the aux map receives v
+//                     rounded to T, C receives gelu of that rounded v
+//   kEpiGeluBackward  d = alpha * acc rounded to T; C = gelu_backward(d, h),
+//                     h read from p.aux
+// The activation math is the elementwise kernels' own (unary_apply /
+// unary_backward_apply, narrow-type fast forms), applied to the same rounded
+// values, so a fused product gives the bits of the product followed by the
+// separate activation kernel.
+constexpr int kEpiPlain = 0;
+constexpr int kEpiGelu = 1;
+constexpr int kEpiGeluBackward = 2;
 
 // Element traits: 128 bytes of K per stage row in every case.
 template <typename T> struct TcElem;
@@ -226,6 +252,26 @@ __device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap* ma
                 if constexpr (BATCHED) tma_load_3d(dst + j * kBoxRows * 128, map, bar, k0, mn0 + j * kBoxRows, b);
                 else tma_load_2d(dst + j * kBoxRows * 128, map, bar, k0, mn0 + j * kBoxRows);
             }
+        }
+    }
+}
+
+// The CTA-pair form of load_operand with an L2 eviction-priority policy.
+template <int ES, bool MN, bool BATCHED>
+__device__ __forceinline__ void load_operand_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar, int mn0, int k0,
+                                                  int b, int rows, uint64_t policy) {
+    constexpr int kEPR = 128 / ES;
+    constexpr uint32_t kChunk = kEPR * 128;
+    if constexpr (MN) {
+        for (int j = 0; j < rows / kEPR; ++j) {
+            if constexpr (BATCHED) tma_load_3d_pair_hint(dst + j * kChunk, map, bar, mn0 + j * kEPR, k0, b, policy);
+            else tma_load_2d_pair_hint(dst + j * kChunk, map, bar, mn0 + j * kEPR, k0, policy);
+        }
+    } else {
+        for (int j = 0; j < rows / kBoxRows; ++j) {
+            if constexpr (BATCHED) tma_load_3d_pair_hint(dst + j * kBoxRows * 128, map, bar, k0, mn0 + j * kBoxRows, b,
+                                                         policy);
+            else tma_load_2d_pair_hint(dst + j * kBoxRows * 128, map, bar, k0, mn0 + j * kBoxRows, policy);
         }
     }
 }
@@ -323,20 +369,78 @@ __device__ __forceinline__ void store_accumulator(const TcParams& p, uint32_t t_
     }
 }
 
+// h[n_base .. n_base + 32) of one row of the activation input, as floats
+// (16-byte vectors when the chunk is inside N on a 16-byte boundary; zero
+// past N).
+template <typename T>
+__device__ __forceinline__ void load_aux_chunk(const TcParams& p, const T* row, int64_t n_base, float (&z)[32],
+                                               uint64_t policy) {
+    constexpr int kPer = 16 / int(sizeof(T));
+    if (n_base + 32 <= p.N && (reinterpret_cast<uintptr_t>(row + n_base) & 15u) == 0) {
+        const uint4* src = reinterpret_cast<const uint4*>(row + n_base);
+#pragma unroll
+        for (int q = 0; q < 32 / kPer; ++q) {
+            const uint4 raw = ld_global_v4_hint(src + q, policy);
+            float f[kPer];
+            unpack_vec(*reinterpret_cast<const Vec<T, kPer>*>(&raw), f);
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) z[q * kPer + j] = f[j];
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) z[j] = n_base + j < p.N ? load_as<float>(row[n_base + j]) : 0.0f;
+    }
+}
+
+// gelu_backward on two lanes: the scalar narrow-type form of
+// unary_backward_apply (Phi(z) + z phi(z) with phi from ex2.approx), each
+// multiply and fused multiply-add as its two-lane instruction, which rounds
+// each lane exactly as the scalar one does.
+__device__ __forceinline__ float2 gelu_backward_narrow2(float2 dy, float2 z) {
+    float2 t = __fmul2_rn(z, z);
+    t = __fmul2_rn(t, f2(-0.72134752044448170368f));
+    float2 e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(t.x));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(t.y));
+    const float2 u = __fmul2_rn(z, f2(0.39894228040143267794f));
+    return __fmul2_rn(dy, __ffma2_rn(u, e, phi_narrow2(z)));
+}
+
+// One 32 x 32 chunk into a warp's staging tile, rows swizzled the way the C
+// tensor map expects (64-byte rows for 16-bit types, 128-byte for fp32), so
+// the 32 lanes' 16-byte writes hit distinct banks.
+template <typename T>
+__device__ __forceinline__ void stage_chunk(uint8_t* stage, int lane, const Vec<T, 32>& packed) {
+    constexpr int kRowBytes = 32 * int(sizeof(T));
+    constexpr int kVecs = kRowBytes / 16;
+    const uint4* src = reinterpret_cast<const uint4*>(&packed);
+    uint8_t* row = stage + lane * kRowBytes;
+#pragma unroll
+    for (int q = 0; q < kVecs; ++q) {
+        const int phys = kRowBytes == 64 ? (q ^ ((lane >> 1) & 3)) : (q ^ (lane & 7));
+        *reinterpret_cast<uint4*>(row + phys * 16) = src[q];
+    }
+}
+
 // The same through shared memory and a TMA store: each chunk of 32 rows x
-// 32 columns is converted into this warp's staging tile (rows swizzled the
-// way the C tensor map expects, so the 32 lanes' 16-byte writes hit distinct
-// banks), then one lane stores the whole tile asynchronously in full lines.
-// TMA clips the tile at M and N.  row0: the warp's first row in C.
-template <typename T, int NCOL, bool BATCHED>
+// 32 columns is converted into this warp's staging tile, then one lane
+// stores the whole tile asynchronously in full lines.  TMA clips the tile at
+// M and N.  row0: the warp's first row in C.  EPI selects the epilogue form
+// (kEpiGelu also stores the pre-activation through tmAux, from a second
+// staging tile at stage2).
+template <typename T, int NCOL, bool BATCHED, int EPI = kEpiPlain>
 __device__ __forceinline__ void store_accumulator_tma(const TcParams& p, const CUtensorMap* tmC, uint8_t* stage,
                                                       uint32_t t_rows, int col0, int b, int64_t gm, int64_t row0,
-                                                      int64_t n_tile0, bool row_ok) {
+                                                      int64_t n_tile0, bool row_ok,
+                                                      const CUtensorMap* tmAux = nullptr,
+                                                      uint8_t* stage2 = nullptr) {
     constexpr int kChunks = NCOL / 32;
-    constexpr int kRowBytes = 32 * int(sizeof(T));  // 64 (16-bit) or 128 (fp32)
-    constexpr int kVecs = kRowBytes / 16;
+    constexpr bool kFast = Narrow<T>::value;
     const int lane = threadIdx.x & 31;
     const T* cin = static_cast<const T*>(p.cin);
+    const T* aux_row = nullptr;
+    if constexpr (EPI == kEpiGeluBackward) aux_row = static_cast<const T*>(p.aux) + gm * p.saux_m;
+    const uint64_t pol = p.l2_stream ? l2_policy_evict_first() : l2_policy_evict_normal();
     uint32_t r[2][32];
     __syncwarp();
     tmem_ld32(t_rows + col0, r[0]);
@@ -351,29 +455,68 @@ __device__ __forceinline__ void store_accumulator_tma(const TcParams& p, const C
         for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(rc[j]);
         if (cin != nullptr && row_ok) add_addend_chunk<T>(p, cin + b * p.sci_b + gm * p.sci_m, n_base, v);
         Vec<T, 32> packed;
+        Vec<T, 32> packed2;
+        if constexpr (EPI == kEpiGelu) {
+            // packed2: the pre-activation, rounded; packed: gelu of it.
+            pack_vec(v, packed2);
+            float h[32];
+            unpack_vec(packed2, h);
+            if constexpr (kFast) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const float2 x = make_float2(h[j], h[j + 1]);
+                    const float2 g = __fmul2_rn(x, phi_narrow2(x));
+                    v[j] = g.x;
+                    v[j + 1] = g.y;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = unary_apply<float, kFast>(TPB_GELU, h[j], 0.0f);
+            }
+        } else if constexpr (EPI == kEpiGeluBackward) {
+            pack_vec(v, packed2);
+            float d[32], z[32];
+            unpack_vec(packed2, d);
+            if (row_ok) {
+                load_aux_chunk<T>(p, aux_row, n_base, z, pol);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) z[j] = 0.0f;
+            }
+            if constexpr (kFast) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const float2 g = gelu_backward_narrow2(make_float2(d[j], d[j + 1]), make_float2(z[j], z[j + 1]));
+                    v[j] = g.x;
+                    v[j + 1] = g.y;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    v[j] = unary_backward_apply<float, kFast>(TPB_GELU_BACKWARD, d[j], z[j], 0.0f);
+                }
+            }
+        }
         pack_vec(v, packed);
-        // The previous store from this staging tile has finished reading it.
+        // The previous stores from this warp's staging tiles have finished
+        // reading them.
         if (lane == 0) bulk_wait_group_read0();
         __syncwarp();
-        const uint4* src = reinterpret_cast<const uint4*>(&packed);
-        uint8_t* row = stage + lane * kRowBytes;
-#pragma unroll
-        for (int q = 0; q < kVecs; ++q) {
-            const int phys = kRowBytes == 64 ? (q ^ ((lane >> 1) & 3)) : (q ^ (lane & 7));
-            *reinterpret_cast<uint4*>(row + phys * 16) = src[q];
-        }
+        stage_chunk<T>(stage, lane, packed);
+        if constexpr (EPI == kEpiGelu) stage_chunk<T>(stage2, lane, packed2);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0 && n_base < p.N && row0 < p.M) {
-            if constexpr (BATCHED) tma_store_3d(tmC, smem_addr(stage), int(n_base), int(row0), b);
-            else tma_store_2d(tmC, smem_addr(stage), int(n_base), int(row0));
+            if constexpr (BATCHED) tma_store_3d_hint(tmC, smem_addr(stage), int(n_base), int(row0), b, pol);
+            else tma_store_2d_hint(tmC, smem_addr(stage), int(n_base), int(row0), pol);
+            if constexpr (EPI == kEpiGelu) tma_store_2d_hint(tmAux, smem_addr(stage2), int(n_base), int(row0), pol);
             bulk_commit_group();
         }
     }
 }
 
 template <typename T, int BN, bool A_MN, bool B_MN, bool BATCHED>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kTcThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC,
                    const TcParams p) {
@@ -650,9 +793,93 @@ constexpr int kPairStages = 6;
 constexpr int kPairBM = 256;  // rows per CTA pair (128 per CTA)
 constexpr int kPairBN = 256;  // columns per CTA pair (each CTA stages 128 of B)
 
-template <typename T>
+// Staging tiles per epilogue warp: two when the epilogue writes two results.
+template <int EPI>
+__host__ __device__ constexpr int staging_tiles() {
+    return EPI == kEpiGelu ? 2 : 1;
+}
+
+template <typename T, int EPI = kEpiPlain>
 constexpr size_t tc2_smem_bytes() {
-    return size_t(kPairStages) * (128 * 128 + 128 * 128) + kEpilogueWarps * staging_bytes<T>() + 1024 + 256;
+    return size_t(kPairStages) * (128 * 128 + 128 * 128) + kEpilogueWarps * staging_tiles<EPI>() * staging_bytes<T>() +
+           1024 + 512;
+}
+
+// Tile scheduling of the CTA-pair kernel.  The leader CTA's scheduler thread
+// decides which tile the pair computes next and publishes it through a ring
+// of kSchedDepth slots (in both CTAs' shared memory) to its consumers: both
+// CTAs' producers, the leader's MMA thread and both CTAs' epilogue warps; -1
+// ends the sequence.  Each slot's "empty" barrier (the leader's) counts
+// those consumers' arrivals.
+constexpr int kSchedDepth = 4;
+constexpr int kSchedConsumers = 2 + 1 + 2 * kEpilogueWarps;
+// The CTA-pair kernel's warps: 0 TMA producer, 1 MMA issuer, 2-9 epilogue,
+// 10 tile scheduler (leader CTA).  352 threads take the same register
+// allocation as 320 (12-warp granularity).
+constexpr int kTc2Threads = 352;
+constexpr int kSchedWarp = 10;
+// Run-time claims are made just in time: the leader's producer asks for the
+// next tile kClaimLead k-blocks before the end of its current one, so a
+// claim's round trip to L2 is hidden behind those loads while the tiles in
+// flight across the device stay one wave of consecutive claims (claiming
+// further ahead spreads them over several waves' worth of operand panels
+// and measured 10-16% slower from the lost L2 reuse).
+constexpr int kClaimLead = 8;
+
+// The next tile of a cluster: in a fixed order (cluster_id + iter *
+// num_clusters) when p.sched is null; otherwise claimed from the counter word
+// p.sched, whose high half holds the epoch of the launch that last claimed
+// (each launch on the word has its own) and low half the claims made in that
+// epoch, so a launch's first claim restarts the count whatever an earlier
+// launch left behind.  Claims arrive in increasing order, so clusters that
+// start late (SMs busy with a concurrent kernel, e.g. a collective) take
+// fewer tiles instead of holding back tiles assigned to them in advance.
+__device__ __forceinline__ int next_pair_tile(const TcParams& p, int cluster_id, int num_clusters, int iter) {
+    if (p.sched == nullptr) {
+        const int64_t t = int64_t(cluster_id) + int64_t(iter) * num_clusters;
+        return t < p.num_tiles ? int(t) : -1;
+    }
+    unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(p.sched);
+    unsigned long long assumed;
+    uint32_t claim;
+    do {
+        assumed = old;
+        claim = uint32_t(assumed >> 32) == p.epoch ? uint32_t(assumed) : 0u;
+        const unsigned long long next = (static_cast<unsigned long long>(p.epoch) << 32) | (claim + 1u);
+        old = atomicCAS(p.sched, assumed, next);
+    } while (old != assumed);
+    return claim < uint32_t(p.num_tiles) ? int(claim) : -1;
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// mbar_wait with cluster-scope acquire (the slot was written by the other
+// CTA of the pair).
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t start = global_ns();
+    while (true) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (global_ns() - start > kWaitNs) {
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void st_cluster_s32(uint32_t cluster_addr, int v) {
+    asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ void tile_coords_pair(const TcParams& p, int tile, int& b, int& mt, int& nt,
@@ -669,10 +896,10 @@ __device__ __forceinline__ void tile_coords_pair(const TcParams& p, int tile, in
     nt = q / gsize;
 }
 
-template <typename T, bool A_MN, bool B_MN, bool BATCHED>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+template <typename T, bool A_MN, bool B_MN, bool BATCHED, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTc2Threads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmC,
+                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmAux,
                     const TcParams p, const int group_m) {
     using E = TcElem<T>;
     constexpr int kStages = kPairStages;
@@ -688,14 +915,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* smem_a = smem;
     uint8_t* smem_b = smem + kStages * kABytes;
-    uint8_t* staging = smem_b + kStages * kBBytes;  // kEpilogueWarps tiles for TMA stores
-    uint64_t* bars = reinterpret_cast<uint64_t*>(staging + kEpilogueWarps * staging_bytes<T>());
+    // kEpilogueWarps x staging_tiles<EPI> tiles for TMA stores
+    uint8_t* staging = smem_b + kStages * kBBytes;
+    uint64_t* bars =
+        reinterpret_cast<uint64_t*>(staging + kEpilogueWarps * staging_tiles<EPI>() * staging_bytes<T>());
     uint64_t* full = bars;
     uint64_t* empty = bars + kStages;
     uint64_t* acc_full = bars + 2 * kStages;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* drain = acc_empty + 2;
-    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(drain + 1);
+    uint64_t* sched_full = drain + 1;
+    uint64_t* sched_empty = sched_full + kSchedDepth;
+    uint64_t* sched_req = sched_empty + kSchedDepth;
+    volatile int* sched_tile = reinterpret_cast<volatile int*>(sched_req + 1);
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(sched_tile + kSchedDepth);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -716,6 +949,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             mbar_init(smem_addr(&acc_empty[a]), 2 * kEpilogueWarps);
         }
         mbar_init(smem_addr(drain), 1);
+        for (int d = 0; d < kSchedDepth; ++d) {
+            mbar_init(smem_addr(&sched_full[d]), 1);
+            mbar_init(smem_addr(&sched_empty[d]), kSchedConsumers);
+        }
+        mbar_init(smem_addr(sched_req), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
@@ -734,15 +972,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ---------------------------------------------------- producer --
         if (lane == 0) {
+            const uint64_t pol_ops = p.l2_operands ? l2_policy_evict_last() : l2_policy_evict_normal();
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int tile = cluster_id; tile < p.num_tiles && ok; tile += num_clusters) {
+            for (int iter = 0; ok; ++iter) {
+                const int slot = iter % kSchedDepth;
+                if (!mbar_wait_cluster(smem_addr(&sched_full[slot]), (iter / kSchedDepth) & 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                const int tile = sched_tile[slot];
+                mbar_arrive_cluster(map_to_cta(smem_addr(&sched_empty[slot]), 0));
+                if (tile < 0) break;
                 int b, mt, nt;
                 tile_coords_pair(p, tile, b, mt, nt, group_m);
                 const int m0 = mt * kPairBM + int(rank) * 128;
                 const int n0 = nt * kPairBN + int(rank) * 128;
+                const int kb_request = leader && p.sched != nullptr ? max(0, p.k_blocks - kClaimLead) : -1;
                 for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (kb == kb_request) mbar_arrive(smem_addr(sched_req));  // claim the next tile now
                     if (!mbar_wait(smem_addr(&empty[stage]), phase ^ 1, abort_flag)) {
                         ok = false;
                         break;
@@ -753,8 +1002,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     const uint32_t da = smem_addr(smem_a + stage * kABytes);
                     const uint32_t db = smem_addr(smem_b + stage * kBBytes);
                     const int k0 = kb * kEPR;
-                    load_operand<E::kES, A_MN, BATCHED, true>(da, &tmA, fb, m0, k0, b, 128);
-                    load_operand<E::kES, B_MN, BATCHED, true>(db, &tmB, fb, n0, k0, b, 128);
+                    load_operand_pair<E::kES, A_MN, BATCHED>(da, &tmA, fb, m0, k0, b, 128, pol_ops);
+                    load_operand_pair<E::kES, B_MN, BATCHED>(db, &tmB, fb, n0, k0, b, 128, pol_ops);
                     if (++stage == kStages) {
                         stage = 0;
                         phase ^= 1;
@@ -774,7 +1023,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             constexpr uint32_t b_lbo = B_MN ? kChunk : 16;
             constexpr uint32_t a_kstep = A_MN ? kUmmaK * 128 : 32;
             constexpr uint32_t b_kstep = B_MN ? kUmmaK * 128 : 32;
-            for (int tile = cluster_id; tile < p.num_tiles && ok; tile += num_clusters, ++local) {
+            for (int iter = 0; ok; ++iter, ++local) {
+                const int slot = iter % kSchedDepth;
+                if (!mbar_wait(smem_addr(&sched_full[slot]), (iter / kSchedDepth) & 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                const int tile = sched_tile[slot];
+                mbar_arrive(smem_addr(&sched_empty[slot]));
+                if (tile < 0) break;
                 const int acc = local & 1;
                 const uint32_t acc_phase = (local >> 1) & 1;
                 if (!mbar_wait(smem_addr(&acc_empty[acc]), acc_phase ^ 1, abort_flag)) {
@@ -815,6 +1072,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if (global_ns() - start > kWaitNs) break;
             }
         }
+    } else if (warp == kSchedWarp) {
+        // ------------------------------------ tile scheduler (leader CTA) --
+        if (leader && lane == 0) {
+            for (int iter = 0;; ++iter) {
+                const int slot = iter % kSchedDepth;
+                if (!mbar_wait(smem_addr(&sched_empty[slot]), ((iter / kSchedDepth) & 1) ^ 1, abort_flag)) {
+                    atomicExch(p.err, kErrProducer);
+                    break;
+                }
+                // Run-time claims wait for the producer's request (made while
+                // it loads the previous tile's last k-blocks).
+                if (p.sched != nullptr && iter > 0 &&
+                    !mbar_wait(smem_addr(sched_req), (iter - 1) & 1, abort_flag)) {
+                    atomicExch(p.err, kErrProducer);
+                    break;
+                }
+                const int tile = next_pair_tile(p, cluster_id, num_clusters, iter);
+                sched_tile[slot] = tile;
+                st_cluster_s32(map_to_cta(smem_addr(const_cast<int*>(&sched_tile[slot])), 1), tile);
+                mbar_arrive(smem_addr(&sched_full[slot]));
+                mbar_arrive_cluster(map_to_cta(smem_addr(&sched_full[slot]), 1));
+                if (tile < 0) break;
+            }
+        }
     } else {
         // ------------------------------------------ epilogue (both CTAs) --
         const int quad = warp & 3;
@@ -823,7 +1104,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         int local = 0;
         const uint32_t leader_empty0 = map_to_cta(smem_addr(&acc_empty[0]), 0);
         const uint32_t leader_empty1 = map_to_cta(smem_addr(&acc_empty[1]), 0);
-        for (int tile = cluster_id; tile < p.num_tiles; tile += num_clusters, ++local) {
+        for (int iter = 0;; ++iter, ++local) {
+            const int slot = iter % kSchedDepth;
+            if (!mbar_wait_cluster(smem_addr(&sched_full[slot]), (iter / kSchedDepth) & 1, abort_flag)) {
+                if (lane == 0) atomicExch(p.err, kErrEpilogue);
+                break;
+            }
+            const int tile = sched_tile[slot];
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_addr(&sched_empty[slot]), 0));
+            if (tile < 0) break;
             const int acc = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
             if (!mbar_wait(smem_addr(&acc_full[acc]), acc_phase, abort_flag)) {
@@ -836,9 +1126,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int64_t gm = int64_t(mt) * kPairBM + row_in_tile;
             const uint32_t t_rows = tmem_base + (uint32_t(quad * 32) << 16) + acc * kPairBN;
             if (p.tma_store) {
-                store_accumulator_tma<T, kPairBN / 2, BATCHED>(p, &tmC, staging + (warp - 2) * staging_bytes<T>(),
-                                                               t_rows, half * (kPairBN / 2), b, gm, gm - lane,
-                                                               int64_t(nt) * kPairBN, gm < p.M);
+                uint8_t* stage = staging + (warp - 2) * staging_tiles<EPI>() * staging_bytes<T>();
+                store_accumulator_tma<T, kPairBN / 2, BATCHED, EPI>(p, &tmC, stage, t_rows, half * (kPairBN / 2), b,
+                                                                    gm, gm - lane, int64_t(nt) * kPairBN, gm < p.M,
+                                                                    &tmAux, stage + staging_bytes<T>());
             } else {
                 store_accumulator<T, kPairBN / 2>(p, t_rows, half * (kPairBN / 2), b, gm, int64_t(nt) * kPairBN,
                                                   gm < p.M);
@@ -864,6 +1155,58 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------ host side --
+
+// Counter words of the run-time tile scheduler: one per (device, stream)
+// slot; a launch's epoch (per slot, counted on the host) tells its claims
+// from those of the launches before it.
+constexpr int kSchedSlots = 64;
+__device__ unsigned long long g_gemm_sched[kSchedSlots];
+
+struct SchedSlot {
+    unsigned long long* word;
+    uint32_t epoch;
+};
+
+// Whether the CTA-pair products on a device claim tiles at run time
+// (tp_b200_set_gemm_tile_order; TPB200_GEMM_SCHED=dynamic turns it on for
+// every device).  The fixed order is the default: it keeps each wave's
+// tiles on neighbouring panels, and claiming costs a round trip per tile.
+std::atomic<bool> g_gemm_dynamic[64] = {};
+
+// The counter word and a fresh epoch for a launch on `stream`, or a null
+// word (fixed tile order) unless run-time claims are on for the device;
+// also while the stream is being captured into a graph (every replay would
+// reuse the recorded epoch), for the per-thread default stream (one handle,
+// many streams) and when the slots are used up.
+SchedSlot gemm_sched_slot(int dev, cudaStream_t stream) {
+    static const bool env_dynamic = [] {
+        const char* e = std::getenv("TPB200_GEMM_SCHED");
+        return e != nullptr && std::strcmp(e, "dynamic") == 0;
+    }();
+    const bool dynamic = dev >= 0 && dev < 64 && (env_dynamic || g_gemm_dynamic[dev].load(std::memory_order_relaxed));
+    if (!dynamic || stream == cudaStreamPerThread) return {nullptr, 0};
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    TPB_CUDA(cudaStreamIsCapturing(stream, &cap));
+    if (cap != cudaStreamCaptureStatusNone) return {nullptr, 0};
+    static std::mutex lock;
+    static unsigned long long* base[64] = {};
+    static std::map<std::pair<int, cudaStream_t>, std::pair<int, uint32_t>> slots;
+    static int used[64] = {};
+    std::lock_guard<std::mutex> g(lock);
+    if (base[dev] == nullptr) {
+        void* ptr = nullptr;
+        TPB_CUDA(cudaGetSymbolAddress(&ptr, g_gemm_sched));
+        base[dev] = static_cast<unsigned long long*>(ptr);
+    }
+    auto it = slots.find({dev, stream});
+    if (it == slots.end()) {
+        if (used[dev] >= kSchedSlots) return {nullptr, 0};
+        it = slots.emplace(std::make_pair(dev, stream), std::make_pair(used[dev]++, 0u)).first;
+    }
+    uint32_t& epoch = it->second.second;
+    if (++epoch == 0) epoch = 1;  // 0 is the words' initial value
+    return {base[dev] + it->second.first, epoch};
+}
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
@@ -966,15 +1309,16 @@ void launch_tc(const GemmProblem& p, const CUtensorMap& ma, const CUtensorMap& m
     tp.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (uint32_t(tp.a_mn) << 15) |
                (uint32_t(tp.b_mn) << 16) | (uint32_t(BN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
     const int grid = std::min(tp.num_tiles, gemm_sm_budget(dev));
-    launch_pdl(kern, grid, kThreads, smem, stream, ma, mb, mc, tp);
+    launch_pdl(kern, grid, kTcThreads, smem, stream, ma, mb, mc, tp);
     check_launch("gemm_tc");
 }
 
-template <typename T, bool A_MN, bool B_MN, bool BATCHED>
+template <typename T, bool A_MN, bool B_MN, bool BATCHED, int EPI = kEpiPlain>
 void launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, TcParams& tp, int dev,
-                cudaStream_t stream) {
-    constexpr size_t smem = tc2_smem_bytes<T>();
-    auto kern = gemm_tc2_kernel<T, A_MN, B_MN, BATCHED>;
+                cudaStream_t stream, const CUtensorMap* maux = nullptr) {
+    constexpr size_t smem = tc2_smem_bytes<T, EPI>();
+    static_assert(smem <= 232448, "shared memory per CTA");
+    auto kern = gemm_tc2_kernel<T, A_MN, B_MN, BATCHED, EPI>;
     static bool configured[64] = {};
     if (!configured[dev]) {
         TPB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
@@ -989,11 +1333,32 @@ void launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
     // Row-tile groups sized so the group's A panels (~32 MiB, a quarter of L2:
     // the two dies each cache their own half) stay resident while B streams
     // past them.
+    // TPB200_GEMM_GROUP_MB overrides the 32 MiB panel budget (A/B measurements).
+    static const int64_t budget_mb = [] {
+        const char* e = std::getenv("TPB200_GEMM_GROUP_MB");
+        const long v = e != nullptr ? std::strtol(e, nullptr, 10) : 0;
+        return v > 0 ? int64_t(v) : int64_t(32);
+    }();
     const int64_t panel = int64_t(kPairBM) * tp.K * int64_t(sizeof(T));
-    int group_m = static_cast<int>(std::max<int64_t>(1, (int64_t(32) << 20) / std::max<int64_t>(panel, 1)));
+    int group_m = static_cast<int>(std::max<int64_t>(1, (budget_mb << 20) / std::max<int64_t>(panel, 1)));
     group_m = std::min(group_m, tp.m_tiles);
     const int clusters = std::min(tp.num_tiles, gemm_sm_budget(dev) / 2);
-    launch_pdl(kern, 2 * clusters, kThreads, smem, stream, ma, mb, mc, tp, group_m);
+    const SchedSlot slot = gemm_sched_slot(dev, stream);
+    tp.sched = slot.word;
+    tp.epoch = slot.epoch;
+    // TPB200_GEMM_L2HINT=none|stream|both (A/B measurements): which accesses
+    // carry an eviction-priority policy.  None by default: in the MLP step,
+    // evict_first on the epilogue's streams measured 4.36 ms per step and
+    // evict_last on the operands as well 4.27 ms, against 4.24 ms without.
+    static const int l2hint = [] {
+        const char* e = std::getenv("TPB200_GEMM_L2HINT");
+        if (e == nullptr || std::strcmp(e, "none") == 0) return 0;
+        if (std::strcmp(e, "both") == 0) return 2;
+        return 1;
+    }();
+    tp.l2_stream = l2hint >= 1 ? 1 : 0;
+    tp.l2_operands = l2hint >= 2 ? 1 : 0;
+    launch_pdl(kern, 2 * clusters, kTc2Threads, smem, stream, ma, mb, mc, maux != nullptr ? *maux : mc, tp, group_m);
     check_launch("gemm_tc2");
 }
 
@@ -1040,10 +1405,36 @@ bool use_pair_kernel(const GemmProblem& p) {
     return p.M >= kPairBM && p.N >= kPairBN;
 }
 
+// The fused-epilogue instances: bf16, unbatched, CTA-pair kernel.
+template <typename T, int EPI>
+void launch_epi(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& maux,
+                TcParams& tp, int dev, cudaStream_t stream) {
+    const int code = (tp.a_mn ? 2 : 0) | (tp.b_mn ? 1 : 0);
+    switch (code) {
+        case 0: launch_tc2<T, false, false, false, EPI>(ma, mb, mc, tp, dev, stream, &maux); break;
+        case 1: launch_tc2<T, false, true, false, EPI>(ma, mb, mc, tp, dev, stream, &maux); break;
+        case 2: launch_tc2<T, true, false, false, EPI>(ma, mb, mc, tp, dev, stream, &maux); break;
+        default: launch_tc2<T, true, true, false, EPI>(ma, mb, mc, tp, dev, stream, &maux); break;
+    }
+}
+
 template <typename T>
 bool gemm_tc_typed(const GemmProblem& p_in, int dev, cudaStream_t stream, CUtensorMapDataType type) {
     constexpr int es = sizeof(T);
     GemmProblem p = p_in;
+    if (p.epi != kEpiPlain) {
+        // Fused epilogues: bf16 products with a full CTA-pair tile, no batch,
+        // the result (and gelu's pre-activation) written by TMA stores.
+        if constexpr (!std::is_same<T, __nv_bfloat16>::value) {
+            return false;
+        } else {
+            if (p.batch != 1 || !use_pair_kernel(p) || p.aux == nullptr) return false;
+            if (p.epi == kEpiGeluBackward && p.cin != nullptr) return false;
+            if (p.epi == kEpiGelu && !(aligned16(p.aux) && p.saux_m > 0 && (p.saux_m * es) % 16 == 0)) return false;
+            if (std::getenv("TPB200_NO_TMA_STORE") != nullptr) return false;
+            if (!(aligned16(p.c) && p.sc_m > 0 && (p.sc_m * es) % 16 == 0)) return false;
+        }
+    }
     // TF32 operands must be K-major here: the 128-byte-swizzled MN-major
     // layout this kernel stages is defined for 16-bit elements only (32-bit
     // MN-major operands need the 32-byte-atom swizzle variant).  An MN-major
@@ -1134,6 +1525,8 @@ bool gemm_tc_typed(const GemmProblem& p_in, int dev, cudaStream_t stream, CUtens
     tp.alpha = static_cast<float>(p.alpha);
     tp.beta = static_cast<float>(p.beta);
     tp.vec_store = aligned16(p.c) && (p.sc_m * es) % 16 == 0 && (p.batch == 1 || (p.sc_b * es) % 16 == 0);
+    tp.aux = p.aux;
+    tp.saux_m = p.saux_m;
     tp.err = device_error_word(dev);
     // The result through a C tensor map (TMA stores) when its layout allows.
     // TPB200_NO_TMA_STORE=1 keeps the direct-store epilogue (A/B measurements).
@@ -1142,6 +1535,18 @@ bool gemm_tc_typed(const GemmProblem& p_in, int dev, cudaStream_t stream, CUtens
                        (p.batch == 1 || (p.sc_b > 0 && (p.sc_b * es) % 16 == 0));
     tp.tma_store = c_tma ? 1 : 0;
     const CUtensorMap mc = c_tma ? make_c_map(p.c, type, es, p.N, p.M, p.sc_m, p.batch, p.sc_b) : ma;
+    if (p.epi != kEpiPlain) {
+        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+            TPB_CHECK(pair && c_tma, "gemm: fused epilogue without the CTA-pair TMA-store kernel");
+            if (p.epi == kEpiGelu) {
+                const CUtensorMap maux = make_c_map(p.aux, type, es, p.N, p.M, p.saux_m, 1, 0);
+                launch_epi<T, kEpiGelu>(ma, mb, mc, maux, tp, dev, stream);
+            } else {
+                launch_epi<T, kEpiGeluBackward>(ma, mb, mc, mc, tp, dev, stream);
+            }
+        }
+        return true;
+    }
     launch_any<T>(pair, bn, p, ma, mb, mc, tp, dev, stream);
     return true;
 }
@@ -1380,6 +1785,7 @@ bool gemm_f32_split(const GemmProblem& p, int dev, cudaStream_t stream) {
 
 bool gemm_tc(const GemmProblem& p, int dev, cudaStream_t stream) {
     if (p.M == 0 || p.N == 0 || p.K == 0) return false;
+    if (p.epi != kEpiPlain && p.dtype != TPB_BF16) return false;
     switch (p.dtype) {
         case TPB_BF16: return gemm_tc_typed<__nv_bfloat16>(p, dev, stream, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
         case TPB_F16: return gemm_tc_typed<__half>(p, dev, stream, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
@@ -1391,3 +1797,10 @@ bool gemm_tc(const GemmProblem& p, int dev, cudaStream_t stream) {
 }
 
 }  // namespace tpb
+
+extern "C" int tp_b200_set_gemm_tile_order(int dev, int dynamic) {
+    return tpb::guarded([&] {
+        TPB_CHECK(dev >= 0 && dev < 64, "invalid device index %d", dev);
+        tpb::g_gemm_dynamic[dev].store(dynamic != 0, std::memory_order_relaxed);
+    });
+}

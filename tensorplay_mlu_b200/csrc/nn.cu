@@ -423,6 +423,63 @@ void with_index_type(int dtype, Fn fn) {
 }
 
 }  // namespace
+// Mean squared error with its gradient in one pass over (out, target):
+//   diff = round(out - target); sq = round(diff * diff); grad = round(diff * s)
+// (round: to the storage type, where the separate sub / pow / mul operators
+// round), per-block fp32 sums of sq (fp64 for fp64), combined in block order
+// by mse_finish: loss = round(sum / n).  V: elements per 16-byte vector (1
+// when a pointer is not 16-byte aligned).
+template <typename T, int V>
+__global__ void __launch_bounds__(kThreads) mse_partials(const T* __restrict__ out, const T* __restrict__ target,
+                                                         T* __restrict__ grad, typename Stat<T>::type* partial,
+                                                         int64_t n, float grad_scale) {
+    pdl_entry();
+    using A = typename Stat<T>::type;
+    using C = typename std::conditional<std::is_same<T, double>::value, double, float>::type;
+    using VT = Vec<T, V>;
+    A acc = A(0);
+    const int64_t nvec = n / V;
+    const int64_t stride = int64_t(gridDim.x) * kThreads;
+    for (int64_t i = int64_t(blockIdx.x) * kThreads + threadIdx.x; i < nvec; i += stride) {
+        const VT o = reinterpret_cast<const VT*>(out)[i];
+        const VT t = reinterpret_cast<const VT*>(target)[i];
+        C fo[V], ft[V], g[V];
+        unpack_vec(o, fo);
+        unpack_vec(t, ft);
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            const C d = load_as<C>(store_as<T>(fo[j] - ft[j]));
+            acc += A(load_as<C>(store_as<T>(d * d)));
+            g[j] = d * C(grad_scale);
+        }
+        if (grad != nullptr) {
+            VT gv;
+            pack_vec(g, gv);
+            reinterpret_cast<VT*>(grad)[i] = gv;
+        }
+    }
+    if (blockIdx.x == 0) {
+        for (int64_t i = nvec * V + threadIdx.x; i < n; i += kThreads) {
+            const C d = load_as<C>(store_as<T>(load_as<C>(out[i]) - load_as<C>(target[i])));
+            acc += A(load_as<C>(store_as<T>(d * d)));
+            if (grad != nullptr) grad[i] = store_as<T>(d * C(grad_scale));
+        }
+    }
+    acc = block_sum(acc);
+    if (threadIdx.x == 0) partial[blockIdx.x] = acc;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) mse_finish(const typename Stat<T>::type* __restrict__ partial, int blocks,
+                                                       T* __restrict__ loss, double n) {
+    pdl_entry();
+    using A = typename Stat<T>::type;
+    A acc = A(0);
+    for (int i = threadIdx.x; i < blocks; i += kThreads) acc += partial[i];
+    acc = block_sum(acc);
+    if (threadIdx.x == 0) loss[0] = store_as<T>(acc / A(n));
+}
+
 }  // namespace tpb
 
 using namespace tpb;
@@ -688,6 +745,52 @@ int tp_b200_masked_scale(const tpb_tensor* dx, const tpb_tensor* dy, const tpb_t
                 static_cast<scalar_t*>(dx->data), n, scale);
         });
         check_launch("masked_scale");
+    });
+}
+
+// The MLP step's loss: mean((out - target)^2) into `loss` (one element of
+// out's dtype) and, when `grad` is not NULL, grad = (out - target) *
+// grad_scale (2 / n for d loss / d out), one read of out and target.
+int tp_b200_mse_loss(const tpb_tensor* loss, const tpb_tensor* grad, const tpb_tensor* out,
+                     const tpb_tensor* target, double grad_scale, void* stream) {
+    return guarded([&] {
+        require_dense(out, "mse_loss input");
+        require_dense(target, "mse_loss target");
+        require_dense(loss, "mse_loss result");
+        if (grad != nullptr) require_dense(grad, "mse_loss gradient");
+        TPB_CHECK(is_floating(out->dtype) && target->dtype == out->dtype && loss->dtype == out->dtype &&
+                      (grad == nullptr || grad->dtype == out->dtype),
+                  "mse_loss: floating operands of one dtype");
+        const int64_t n = numel_of(*out);
+        TPB_CHECK(numel_of(*target) == n && (grad == nullptr || numel_of(*grad) == n),
+                  "mse_loss: input, target and gradient sizes differ");
+        TPB_CHECK(numel_of(*loss) == 1, "mse_loss: the result is one element");
+        TPB_CHECK(n > 0, "mse_loss: empty input");
+        const int dev = device_of(out->data);
+        DeviceGuard guard(dev);
+        cudaStream_t s = resolve_stream(stream, dev);
+        const int blocks = static_cast<int>(std::max<int64_t>(
+            1, std::min<int64_t>(blocks_for((n + 7) / 8, kThreads), int64_t(num_sms(dev)) * 4)));
+        TPB_DISPATCH_FLOAT(out->dtype, "mse_loss", {
+            using A = typename Stat<scalar_t>::type;
+            constexpr int V = VecWidth<scalar_t>::value;
+            Scratch partial(sizeof(A) * size_t(blocks), dev, s);
+            const scalar_t* o = static_cast<const scalar_t*>(out->data);
+            const scalar_t* t = static_cast<const scalar_t*>(target->data);
+            scalar_t* g = grad != nullptr ? static_cast<scalar_t*>(grad->data) : nullptr;
+            const bool vec = aligned16(o) && aligned16(t) && (g == nullptr || aligned16(g));
+            if (vec) {
+                launch_pdl(mse_partials<scalar_t, V>, blocks, kThreads, 0, s, o, t, g,
+                           static_cast<A*>(partial.get()), n, static_cast<float>(grad_scale));
+            } else {
+                launch_pdl(mse_partials<scalar_t, 1>, blocks, kThreads, 0, s, o, t, g,
+                           static_cast<A*>(partial.get()), n, static_cast<float>(grad_scale));
+            }
+            check_launch("mse_partials");
+            launch_pdl(mse_finish<scalar_t>, 1, kThreads, 0, s, static_cast<const A*>(partial.get()), blocks,
+                       static_cast<scalar_t*>(loss->data), static_cast<double>(n));
+            check_launch("mse_finish");
+        });
     });
 }
 

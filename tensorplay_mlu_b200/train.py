@@ -4,19 +4,37 @@ The model of tensorplay-mlu's README distributed benchmark, at the sizes the
 B200 build is measured on: Linear(4096 -> 16384), GELU, Linear(16384 -> 4096),
 bf16 weights with PyTorch's nn.Linear initialisation (Kaiming-uniform, bound
 1/sqrt(fan_in)) from seed 0, loss = mean((out - target)^2), full backward
-(no input gradient) and an SGD update.  Every step is a sequence of the
-backend's own operators -- the ones TensorPlay's autograd engine would call
-for this model (linear, gelu, sub, pow, mean, mul, mm on transposed views,
-sum over dim 0, gelu_backward, add_) -- so the step exercises the claimed
-kernels end to end.
+(no input gradient) and an SGD update.  The step computes what TensorPlay's
+autograd engine computes for this model with its operators (linear, gelu,
+sub, pow, mean, mul, mm on transposed views, sum over dim 0, gelu_backward,
+add_), rounding every intermediate where those operators round, with the
+memory-bound operators fused into their producers:
+
+  h = x W1^T + b1, a = gelu(h)      one product, gelu in its epilogue
+                                    (h kept for the backward pass)
+  out = a W2^T + b2                 product, bias in the epilogue
+  loss, d_out = mse(out, t)         one pass: sub, pow, mean and the 2/n mul
+  dW2 = d_out^T a, db2 = sum(d_out) product (transposes read in place), sum
+  d_h = gelu_backward(d_out W2, h)  one product, gelu_backward in its epilogue
+  dW1 = d_h^T x, db1 = sum(d_h)     product, sum
+  p += -lr * g                      one launch per gradient bucket (the
+                                    parameters share the gradients' layout)
 
 Data parallelism (one rank per GPU): gradients live in one flat buffer split
-into two buckets in backward order, (dW2, db2) then (dW1, db1).  Each bucket
-is all-reduced (SUM) on a side stream as soon as backward has produced it,
-so the first exchange overlaps the dh / dW1 GEMMs (the GEMM running beside
-it leaves `comm_sms` SMs to the collective's kernels); the AVG's 1/world scale is
-folded into the SGD step (p -= lr/world * g_sum), not launched as its own
-pass as tensorplay_mlu/distributed.py:241-242 does.
+into two buckets in backward order, A = (dW2, db2) and B = (db1, dW1), and
+the parameters in one flat buffer of the same layout.  Each bucket is
+all-reduced (SUM) on a side stream as soon as backward has produced it:
+bucket A beside the d_h and dW1 products; bucket B in `dw1_slices` row
+slices of dW1 (db1 travels with the first), each slice's exchange beside
+the next slice's product.  With `overlap_next_step` the SGD update of
+bucket B's slices is deferred into the next step, each slice applied just
+before the next step's h = x W1^T product for the same rows of W1, which
+runs slice by slice -- so no exchange waits after the last product of a
+step; `flush()` applies what is still pending.  The tensor-core products
+claim their tiles at run time, so SMs taken by the collective's kernels
+delay no tiles.  The AVG's 1/world scale is folded into the SGD step
+(p -= lr/world * g_sum), not launched as its own pass as
+tensorplay_mlu/distributed.py:241-242 does.
 """
 
 from __future__ import annotations
@@ -39,15 +57,18 @@ class MLPConfig:
     batch: int = 8192
     lr: float = 1e-3
     dtype: torch.dtype = torch.bfloat16
-    # Data-parallel: the last gradient bucket (dW1, db1) is produced and
-    # all-reduced in this many row slices, so each slice's exchange overlaps
-    # the next slice's GEMM.
-    dw1_slices: int = 1
+    # Data-parallel: the last gradient bucket (db1, dW1) is produced and
+    # all-reduced in this many row slices of dW1, so each slice's exchange
+    # overlaps the next slice's product.
+    dw1_slices: int = 2
+    # Data-parallel: defer bucket B's SGD update into the next step, slice by
+    # slice ahead of that step's first product (call flush() after the last
+    # step).  False: every step ends with its parameters updated.
+    overlap_next_step: bool = False
     # Data-parallel: SMs left free for the collective's kernels while the
-    # d_a GEMM overlaps the first bucket's all-reduce (the GEMM is persistent
-    # with statically scheduled tiles, so SMs taken by the collective would
-    # otherwise delay its last tiles).  0: the GEMM takes every SM.
-    comm_sms: int = 32
+    # d_h product overlaps bucket A's all-reduce.  0 (default): the product
+    # takes every SM, its tiles claimed at run time.
+    comm_sms: int = 0
 
 
 def init_params_host(cfg: MLPConfig, seed: int = 0):
@@ -83,22 +104,29 @@ class DataParallelMLP:
         self.world = pg.size() if pg is not None else 1
         w1, b1, w2, b2 = host_params if host_params is not None else init_params_host(cfg)
         dev = self.device
-        # Parameters.
-        self.w1 = ops.to_device(w1, dev)
-        self.b1 = ops.to_device(b1, dev)
-        self.w2 = ops.to_device(w2, dev)
-        self.b2 = ops.to_device(b2, dev)
-        # One flat gradient buffer, bucket A = (dW2, db2), bucket B = (dW1, db1).
+        # One flat gradient buffer, bucket A = (dW2, db2), bucket B = (dW1,
+        # db1), and one flat parameter buffer with the same layout, so the
+        # SGD update of a bucket is one launch over one slice.
         H, D = cfg.d_hidden, cfg.d_in
         n_a = D * H + D
         n_b = H * D + H
+        self.n_a = n_a
         self.grad_flat = torch.empty(n_a + n_b, dtype=cfg.dtype, device=dev)
+        self.param_flat = torch.empty(n_a + n_b, dtype=cfg.dtype, device=dev)
         self.bucket_a = self.grad_flat.narrow(0, 0, n_a)
         self.bucket_b = self.grad_flat.narrow(0, n_a, n_b)
         self.dw2 = self.bucket_a.narrow(0, 0, D * H).view(D, H)
         self.db2 = self.bucket_a.narrow(0, D * H, D)
-        self.dw1 = self.bucket_b.narrow(0, 0, H * D).view(H, D)
-        self.db1 = self.bucket_b.narrow(0, H * D, H)
+        self.db1 = self.bucket_b.narrow(0, 0, H)
+        self.dw1 = self.bucket_b.narrow(0, H, H * D).view(H, D)
+        self.params_a = self.param_flat.narrow(0, 0, n_a)
+        self.params_b = self.param_flat.narrow(0, n_a, n_b)
+        self.w2 = self.params_a.narrow(0, 0, D * H).view(D, H)
+        self.b2 = self.params_a.narrow(0, D * H, D)
+        self.b1 = self.params_b.narrow(0, 0, H)
+        self.w1 = self.params_b.narrow(0, H, H * D).view(H, D)
+        for dst, src in ((self.w1, w1), (self.b1, b1), (self.w2, w2), (self.b2, b2)):
+            ops.copy_(dst, ops.to_device(src.contiguous(), dev))
         self.comm_stream = torch.cuda.Stream(device=dev) if pg is not None and self.world > 1 else None
         # TPB200_COMM_SMS overrides cfg.comm_sms (A/B measurements).
         reserve = int(os.environ.get("TPB200_COMM_SMS", cfg.comm_sms))
@@ -109,6 +137,10 @@ class DataParallelMLP:
         self.gemm_events: Optional[list] = None
         # When a dict, the step stores its intermediates in it (for checks).
         self.trace: Optional[dict] = None
+        # Bucket B slices whose SGD update is deferred: (start, length, work).
+        self._pending: list = []
+        bounds = [(H * i // max(1, cfg.dw1_slices)) // 8 * 8 for i in range(max(1, cfg.dw1_slices))] + [H]
+        self._slices = [(bounds[i], bounds[i + 1]) for i in range(len(bounds) - 1) if bounds[i + 1] > bounds[i]]
 
     def _timed(self, fn, *args):
         if self.gemm_events is None:
@@ -138,6 +170,22 @@ class DataParallelMLP:
                                        N.stream_of(x.device)), "sum")
         return out
 
+    @staticmethod
+    def _gemm_epilogue(epilogue, out, aux, a, b, c=None):
+        """out (and aux) from a @ b with gelu / gelu_backward fused in."""
+        N.check(N.lib().tp_b200_gemm_epilogue(epilogue, N.describe(out), N.describe(aux), N.describe(a),
+                                              N.describe(b), N.describe(c) if c is not None else None, 1.0,
+                                              1.0 if c is not None else 0.0, 0, N.stream_of(out.device)),
+                "gemm_epilogue")
+        return out
+
+    @staticmethod
+    def _mse_into(loss, grad, out, target):
+        """loss = mean((out - target)^2), grad = 2 (out - target) / numel."""
+        N.check(N.lib().tp_b200_mse_loss(N.describe(loss), N.describe(grad), N.describe(out), N.describe(target),
+                                         2.0 / out.numel(), N.stream_of(out.device)), "mse_loss")
+        return loss
+
     def _gemm_sm_limit(self, sms: int) -> None:
         N.check(N.lib().tp_b200_set_gemm_sm_limit(self.device.index, sms), "set_gemm_sm_limit")
 
@@ -151,14 +199,23 @@ class DataParallelMLP:
     def step(self, x: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
         """One forward + backward + SGD step; returns the loss (device 0-d tensor)."""
         cfg = self.cfg
-        # forward
-        h = self._timed(ops.linear, x, self.w1, self.b1)
-        a = ops.gelu(h)
+        B, D, H = x.shape[0], cfg.d_in, cfg.d_hidden
+        dt, dev = cfg.dtype, x.device
+        # forward: h = x W1^T + b1 and a = gelu(h) from one product
+        h = torch.empty((B, H), dtype=dt, device=dev)
+        a = torch.empty((B, H), dtype=dt, device=dev)
+        if self._pending:
+            # The previous step's bucket B, slice by slice: update the rows of
+            # W1 (and b1, first slice) once their exchange is in, then the
+            # columns of h and a those rows produce.
+            self._timed(self._forward_sliced, x, h, a)
+        else:
+            self._timed(self._gemm_epilogue, N.EPI_GELU, a, h, x, self.w1.t(), self.b1)
         out = self._timed(ops.linear, a, self.w2, self.b2)
-        diff = ops.sub_Tensor(out, target)
-        loss = ops.mean(ops.pow_Tensor_Scalar(diff, 2))
-        # backward of mean((out - t)^2): d out = 2 (out - t) / numel
-        d_out = ops.mul_Scalar(diff, 2.0 / diff.numel())
+        # loss = mean((out - t)^2) and d out = 2 (out - t) / numel in one pass
+        loss = torch.empty((), dtype=dt, device=dev)
+        d_out = torch.empty_like(out)
+        self._mse_into(loss, d_out, out, target)
         self._timed(self._mm_into, self.dw2, d_out.t(), a)
         self._colsum_into(self.db2, d_out)
         work_a = None
@@ -166,61 +223,80 @@ class DataParallelMLP:
             ev = torch.cuda.Event()
             ev.record()
             work_a = self._allreduce_async(self.bucket_a, ev)
+        # d_h = gelu_backward(d_out W2, h) from one product
+        d_h = torch.empty((B, H), dtype=dt, device=dev)
         if self._overlap_sms:
             self._gemm_sm_limit(self._overlap_sms)
             try:
-                d_a = self._timed(ops.mm, d_out, self.w2)
+                self._timed(self._gemm_epilogue, N.EPI_GELU_BACKWARD, d_h, h, d_out, self.w2)
             finally:
                 self._gemm_sm_limit(0)
         else:
-            d_a = self._timed(ops.mm, d_out, self.w2)
-        d_h = ops.gelu_backward(d_a, h)
+            self._timed(self._gemm_epilogue, N.EPI_GELU_BACKWARD, d_h, h, d_out, self.w2)
         if self.trace is not None:
-            self.trace.update(x=x, t=target, h=h, a=a, out=out, d_out=d_out, d_a=d_a, d_h=d_h, loss=loss)
+            self.trace.update(x=x, t=target, h=h, a=a, out=out, d_out=d_out, d_h=d_h, loss=loss)
         if self.comm_stream is None:
             self._timed(self._mm_into, self.dw1, d_h.t(), x)
             self._colsum_into(self.db1, d_h)
-            # SGD: p += -lr * g
-            for p, g in zip(self.params(), self.grads()):
-                ops.add__Tensor(p, g, alpha=-cfg.lr)
+            # SGD: p += -lr * g over the whole flat buffer
+            ops.add__Tensor(self.param_flat, self.grad_flat, alpha=-cfg.lr)
             return loss
-        # Bucket B in row slices of dW1 (db1 travels with the last slice);
-        # each slice's SUM all-reduce starts once its GEMM is done.
+        # Bucket B in row slices of dW1 (db1 travels with the first); each
+        # slice's SUM all-reduce starts once its product is done.
         self._colsum_into(self.db1, d_h)
-        works_b = self._dw1_sliced(d_h, x)
-        # SGD: p += (-lr / world) * g_sum, W2/b2 as soon as bucket A is in.
-        scale = -cfg.lr / self.world
+        pending = self._dw1_sliced(d_h, x)
+        # SGD: p += (-lr / world) * g_sum, bucket A as soon as it is in.
         work_a.wait()
-        ops.add__Tensor(self.w2, self.dw2, alpha=scale)
-        ops.add__Tensor(self.b2, self.db2, alpha=scale)
-        for w in works_b:
-            w.wait()
-        ops.add__Tensor(self.w1, self.dw1, alpha=scale)
-        ops.add__Tensor(self.b1, self.db1, alpha=scale)
+        ops.add__Tensor(self.params_a, self.bucket_a, alpha=self._sgd_scale())
+        self._pending = pending
+        if not cfg.overlap_next_step:
+            self.flush()
         return loss
 
+    def _sgd_scale(self) -> float:
+        return -self.cfg.lr / self.world
+
+    def flush(self) -> None:
+        """Apply the SGD update of every bucket-B slice still pending (the
+        last step's, with overlap_next_step); a no-op otherwise."""
+        for start, length, work in self._pending:
+            work.wait()
+            ops.add__Tensor(self.params_b.narrow(0, start, length), self.bucket_b.narrow(0, start, length),
+                            alpha=self._sgd_scale())
+        self._pending = []
+
+    def _forward_sliced(self, x, h, a):
+        """h = x W1^T + b1 and a = gelu(h) in the column slices matching the
+        pending bucket-B slices, each after its slice's update."""
+        for (start, length, work), (r0, r1) in zip(self._pending, self._slices):
+            work.wait()
+            ops.add__Tensor(self.params_b.narrow(0, start, length), self.bucket_b.narrow(0, start, length),
+                            alpha=self._sgd_scale())
+            self._gemm_epilogue(N.EPI_GELU, a[:, r0:r1], h[:, r0:r1], x, self.w1[r0:r1].t(), self.b1[r0:r1])
+        self._pending = []
+
     def _dw1_sliced(self, d_h, x):
-        """dW1 = d_h^T x as `dw1_slices` row slices (one timed GEMM region),
-        each slice's all-reduce issued as soon as the slice is written."""
-        H, D = self.cfg.d_hidden, self.cfg.d_in
-        n = max(1, int(self.cfg.dw1_slices))
-        bounds = [(H * i // n) // 8 * 8 for i in range(n)] + [H]  # 16-byte-aligned column offsets of d_h
-        works = []
+        """dW1 = d_h^T x in row slices (one timed GEMM region), each slice's
+        all-reduce issued as soon as the slice is written; returns the
+        slices as (offset in bucket B, length, work)."""
+        H = self.cfg.d_hidden
+        D = self.cfg.d_in
+        pending = []
         start = end = None
         if self.gemm_events is not None:
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             start.record()
-        for i in range(n):
-            r0, r1 = bounds[i], bounds[i + 1]
+        for i, (r0, r1) in enumerate(self._slices):
             self._mm_into(self.dw1[r0:r1], d_h[:, r0:r1].t(), x)
             ev = torch.cuda.Event()
             ev.record()
-            length = (r1 - r0) * D if i < n - 1 else self.bucket_b.numel() - r0 * D  # + db1
-            works.append(self._allreduce_async(self.bucket_b.narrow(0, r0 * D, length), ev))
+            lo = 0 if i == 0 else H + r0 * D  # db1 travels with the first slice
+            length = H + r1 * D - lo
+            pending.append((lo, length, self._allreduce_async(self.bucket_b.narrow(0, lo, length), ev)))
         if start is not None:
             end.record()
             self.gemm_events.append((start, end))
-        return works
+        return pending
 
     def flops_per_step(self) -> float:
         """Five GEMMs of 2 * B * D * H each (forward 2, backward 3, no dX)."""

@@ -64,14 +64,41 @@ def _worker(rank: int, port: int, result_dir: str) -> None:
     b = ops.to_device(torch.tensor([float(rank + 7)]))
     pg.broadcast([b], 1).wait()
     out["broadcast"] = ops.to_host(b).tolist()
-    # one DP step of a small MLP
-    cfg = MLPConfig(d_in=256, d_hidden=512, batch=64, lr=0.1)
-    params = init_params_host(cfg, seed=0)
-    model = DataParallelMLP(cfg, device=rank, pg=pg, host_params=params)
-    xh, th = make_batch_host(cfg, seed=rank)
-    model.step(ops.to_device(xh), ops.to_device(th))
-    torch.cuda.synchronize()
-    out["params"] = [ops.to_host(p) for p in model.params()]
+    # gather / gather_single / scatter to and from rank 1, and the coalesced forms
+    g_in = ops.to_device(torch.tensor([10.0 + rank, 20.0 + rank]))
+    g_out = [torch.zeros(2, device="cuda") for _ in range(WORLD)]
+    pg.gather([g_out], [g_in], 1).wait(timeout=60)
+    out["gather_list"] = [ops.to_host(t).tolist() for t in g_out]
+    g_flat = torch.zeros(2 * WORLD, device="cuda")
+    pg.gather_single(g_flat, g_in, 1).wait()
+    out["gather_single"] = ops.to_host(g_flat).tolist()
+    s_in = [ops.to_device(torch.tensor([100.0 * r + rank])) for r in range(WORLD)]
+    s_out = torch.zeros(1, device="cuda")
+    pg.scatter([s_out], [s_in], 1).wait()
+    out["scatter"] = ops.to_host(s_out).tolist()
+    c_in = [ops.to_device(torch.tensor([1.0 + rank])), ops.to_device(torch.tensor([5.0, 6.0]) * (rank + 1))]
+    c_out = [[torch.zeros(1, device="cuda"), torch.zeros(2, device="cuda")] for _ in range(WORLD)]
+    pg.allgather_coalesced(c_out, c_in).wait()
+    out["allgather_coalesced"] = [[ops.to_host(t).tolist() for t in r] for r in c_out]
+    singles = [torch.zeros(WORLD, device="cuda"), torch.zeros(2 * WORLD, device="cuda")]
+    pg.all_gather_single_coalesced(singles, c_in).wait()
+    out["all_gather_single_coalesced"] = [ops.to_host(t).tolist() for t in singles]
+    rs_in = [ops.to_device(torch.arange(WORLD, dtype=torch.float32) + rank),
+             ops.to_device(torch.arange(2 * WORLD, dtype=torch.float32) * (rank + 1))]
+    rs_out = [torch.zeros(1, device="cuda"), torch.zeros(2, device="cuda")]
+    pg.reduce_scatter_single_coalesced(rs_out, rs_in, ReduceOp.SUM).wait()
+    out["reduce_scatter_single_coalesced"] = [ops.to_host(t).tolist() for t in rs_out]
+    # two DP steps of a small MLP, in both schedules of the last bucket
+    for overlap in (False, True):
+        cfg = MLPConfig(d_in=256, d_hidden=512, batch=64, lr=0.1, dw1_slices=2, overlap_next_step=overlap)
+        params = init_params_host(cfg, seed=0)
+        model = DataParallelMLP(cfg, device=rank, pg=pg, host_params=params)
+        xh, th = make_batch_host(cfg, seed=rank)
+        for _ in range(2):
+            model.step(ops.to_device(xh), ops.to_device(th))
+        model.flush()
+        torch.cuda.synchronize()
+        out[f"params_overlap{int(overlap)}"] = [ops.to_host(p) for p in model.params()]
     pg.barrier().wait()
     torch.cuda.synchronize()
     pg.destroy()
@@ -99,10 +126,25 @@ def test_two_rank_collectives_and_dp_step(backend, tmp_path):
         assert r["broadcast"] == [8.0]
     assert r0["reduce_scatter"] == [100.0, 102.0] and r1["reduce_scatter"] == [104.0, 106.0]
     assert r0["all_to_all"] == [0.0, 10.0] and r1["all_to_all"] == [1.0, 11.0]
-    # Both ranks hold identical parameters, equal to the single-GPU step on
-    # the concatenated batch.
-    for a, b in zip(r0["params"], r1["params"]):
+    # tensorplay_mlu/distributed.py:328-470
+    assert r1["gather_list"] == [[10.0, 20.0], [11.0, 21.0]]
+    assert r1["gather_single"] == [10.0, 20.0, 11.0, 21.0]
+    assert r0["scatter"] == [1.0] and r1["scatter"] == [101.0]
+    for r in (r0, r1):
+        assert r["allgather_coalesced"] == [[[1.0], [5.0, 6.0]], [[2.0], [10.0, 12.0]]]
+        assert r["all_gather_single_coalesced"] == [[1.0, 2.0], [5.0, 6.0, 10.0, 12.0]]
+    # rank r gets elements [r] of (arange(2) + 0) + (arange(2) + 1), and
+    # [2r, 2r + 2) of arange(4) * 1 + arange(4) * 2
+    assert r0["reduce_scatter_single_coalesced"] == [[1.0], [0.0, 3.0]]
+    assert r1["reduce_scatter_single_coalesced"] == [[3.0], [6.0, 9.0]]
+    # Both ranks hold identical parameters, equal to the single-GPU steps on
+    # the concatenated batch, in both schedules.
+    for key in ("params_overlap0", "params_overlap1"):
+        for a, b in zip(r0[key], r1[key]):
+            assert torch.equal(a, b)
+    for a, b in zip(r0["params_overlap0"], r0["params_overlap1"]):
         assert torch.equal(a, b)
+    r0["params"] = r0["params_overlap0"]
     from tensorplay_mlu_b200.train import DataParallelMLP, MLPConfig, init_params_host, make_batch_host
 
     ops = backend.ops
@@ -112,7 +154,8 @@ def test_two_rank_collectives_and_dp_step(backend, tmp_path):
     x1, t1 = make_batch_host(cfg, seed=1)
     big = MLPConfig(d_in=256, d_hidden=512, batch=128, lr=0.1)
     single = DataParallelMLP(big, device=0, host_params=params)
-    single.step(ops.to_device(torch.cat([x0, x1])), ops.to_device(torch.cat([t0, t1])))
+    for _ in range(2):
+        single.step(ops.to_device(torch.cat([x0, x1])), ops.to_device(torch.cat([t0, t1])))
     for got, want in zip(r0["params"], single.params()):
         want = ops.to_host(want).float()
         err = (got.float() - want).abs().max().item()
