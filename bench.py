@@ -556,8 +556,11 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     ops = tpb.ops
     host = HostGroup(rank, world)
     hbm_peak, bf16_peak, bf16_sustained, peak_kind = peaks()
-    pg = D.create(_PrefixStore("nccl_b200", host.store), rank, world, device=local, timeout_s=300) \
-        if world > 1 else None
+    # The training step's collectives take at most as many CTAs as the
+    # products beside them leave SMs free (MLPConfig.comm_sms; TPB200_COMM_SMS).
+    comm_sms = int(os.environ.get("TPB200_COMM_SMS", MLPConfig.comm_sms))
+    pg = D.create(_PrefixStore("nccl_b200", host.store), rank, world, device=local, timeout_s=300,
+                  max_ctas=comm_sms) if world > 1 else None
 
     # Kernel-level extras (op sweep, GEMM set) at N = 1: measured before the
     # training loop by default, so their kernels run at the clocks a kernel
@@ -728,7 +731,11 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                                     "than h2d_only_ms_per_step"},
             "dp_params_identical": params_identical,
             "dp_schedule": {"dw1_slices": cfg.dw1_slices, "overlap_next_step": cfg.overlap_next_step,
-                            "gemm_sm_reserve": cfg.comm_sms} if world > 1 else None,
+                            "gemm_sms_beside_collective": model._overlap_sms or None,
+                            "dynamic_tiles_beside_collective": model._overlap_dynamic,
+                            "nccl_max_ctas": comm_sms or None,
+                            "nccl_env": {k: v for k, v in os.environ.items() if k.startswith("NCCL_")}}
+            if world > 1 else None,
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
         }
@@ -736,7 +743,12 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     if pg is not None:
         torch.cuda.synchronize()
         if not args.no_extras:
-            sweep = collective_sweep(pg, host, ops, world)
+            # The sweep measures NCCL unbounded, on a communicator of its own.
+            sweep_pg = D.create(_PrefixStore("nccl_b200_sweep", host.store), rank, world, device=local,
+                                timeout_s=300, group_name="sweep")
+            sweep = collective_sweep(sweep_pg, host, ops, world)
+            torch.cuda.synchronize()
+            sweep_pg.destroy()
             if rank == 0:
                 line["collectives"] = sweep
                 # The largest size of each row, last in the line.

@@ -416,6 +416,13 @@ int tp_b200_nccl_comm_init(int rank, int nranks, int dev, const void* id,
  * instead of waiting for absent ranks.  No reference counterpart. */
 int tp_b200_nccl_comm_init_timeout(int rank, int nranks, int dev, const void* id,
                                    int timeout_ms, void** comm_out);
+/* tp_b200_nccl_comm_init_timeout with bounds on the CTAs (hence SMs) the
+ * communicator's kernels occupy (ncclConfig_t minCTAs / maxCTAs; 0 keeps
+ * NCCL's choice).  No reference counterpart: a data-parallel step whose
+ * products leave a fixed number of SMs free beside a collective caps the
+ * collective at that many. */
+int tp_b200_nccl_comm_init_ctas(int rank, int nranks, int dev, const void* id, int timeout_ms,
+                                int min_ctas, int max_ctas, void** comm_out);
 int tp_b200_nccl_comm_destroy(void* comm);                       /* Cncl.cpp:123-135 */
 int tp_b200_nccl_comm_abort(void* comm);                         /* Cncl.cpp:137-149 */
 int tp_b200_nccl_comm_rank(void* comm, int* rank_out);           /* Cncl.cpp:152-163 */

@@ -145,6 +145,7 @@ _SIGNATURES = {
     "tp_b200_nccl_get_unique_id": ([_P], _I),
     "tp_b200_nccl_comm_init": ([_I, _I, _I, _P, ctypes.POINTER(_P)], _I),
     "tp_b200_nccl_comm_init_timeout": ([_I, _I, _I, _P, _I, ctypes.POINTER(_P)], _I),
+    "tp_b200_nccl_comm_init_ctas": ([_I, _I, _I, _P, _I, _I, _I, ctypes.POINTER(_P)], _I),
     "tp_b200_nccl_comm_destroy": ([_P], _I),
     "tp_b200_nccl_comm_abort": ([_P], _I),
     "tp_b200_nccl_comm_rank": ([_P, ctypes.POINTER(_I)], _I),

@@ -153,7 +153,14 @@ int tp_b200_nccl_comm_init(int rank, int nranks, int dev, const void* id, void**
 
 int tp_b200_nccl_comm_init_timeout(int rank, int nranks, int dev, const void* id, int timeout_ms,
                                    void** comm_out) {
+    return tp_b200_nccl_comm_init_ctas(rank, nranks, dev, id, timeout_ms, 0, 0, comm_out);
+}
+
+int tp_b200_nccl_comm_init_ctas(int rank, int nranks, int dev, const void* id, int timeout_ms, int min_ctas,
+                                int max_ctas, void** comm_out) {
     return nccl_guarded([&] {
+        TPB_CHECK(min_ctas >= 0 && max_ctas >= 0 && (max_ctas == 0 || min_ctas <= max_ctas),
+                  "NCCL: invalid CTA bounds [%d, %d]", min_ctas, max_ctas);
         TPB_CHECK(comm_out != nullptr, "NCCL: null output communicator");
         TPB_CHECK(rank >= 0 && rank < nranks, "NCCL: rank %d out of [0, %d)", rank, nranks);
         TPB_CHECK(id != nullptr, "NCCL: null unique id");
@@ -162,6 +169,8 @@ int tp_b200_nccl_comm_init_timeout(int rank, int nranks, int dev, const void* id
         memcpy(&uid, id, sizeof(uid));
         ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
         config.blocking = 0;
+        if (min_ctas > 0) config.minCTAs = min_ctas;
+        if (max_ctas > 0) config.maxCTAs = max_ctas;
         ncclComm_t comm = nullptr;
         ncclResult_t status = ncclCommInitRankConfig(&comm, nranks, uid, rank, &config);
         const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms);

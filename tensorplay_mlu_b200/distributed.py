@@ -165,7 +165,7 @@ class ProcessGroupB200:
     """Collective provider for one ``nccl_b200`` group (one rank per GPU)."""
 
     def __init__(self, store, rank: int, size: int, device: Optional[int] = None,
-                 group_name: str = "default", timeout_s: float = 300.0) -> None:
+                 group_name: str = "default", timeout_s: float = 300.0, max_ctas: int = 0) -> None:
         self._store = store
         self._rank = rank
         self._size = size
@@ -174,6 +174,8 @@ class ProcessGroupB200:
         self._timeout_s = timeout_s
         self._comm: Optional[ctypes.c_void_p] = None
         self._barrier_flag: Optional[torch.Tensor] = None
+        # Bound on the CTAs (SMs) NCCL's kernels take (0: NCCL's choice).
+        self._max_ctas = int(max_ctas)
 
     # -- lifecycle ---------------------------------------------------------
     def rank(self) -> int:
@@ -198,8 +200,8 @@ class ProcessGroupB200:
             buf = ctypes.create_string_buffer(bytes.fromhex(raw.decode() if isinstance(raw, bytes) else raw), nbytes)
         comm = ctypes.c_void_p()
         timeout_ms = int(self._timeout_s * 1000)
-        _check(lib.tp_b200_nccl_comm_init_timeout(self._rank, self._size, self._device, buf,
-                                                  timeout_ms, ctypes.byref(comm)))
+        _check(lib.tp_b200_nccl_comm_init_ctas(self._rank, self._size, self._device, buf, timeout_ms, 0,
+                                               self._max_ctas, ctypes.byref(comm)))
         self._comm = comm
 
     def destroy(self) -> None:
@@ -648,9 +650,10 @@ def is_available() -> bool:
 
 
 def create(store, rank: int, size: int, device: Optional[int] = None, group_name: str = "default",
-           timeout_s: float = 300.0) -> ProcessGroupB200:
-    """A ready process group (communicator created)."""
-    pg = ProcessGroupB200(store, rank, size, device, group_name, timeout_s)
+           timeout_s: float = 300.0, max_ctas: int = 0) -> ProcessGroupB200:
+    """A ready process group (communicator created); `max_ctas` bounds the
+    SMs its collectives' kernels occupy (0: NCCL's choice)."""
+    pg = ProcessGroupB200(store, rank, size, device, group_name, timeout_s, max_ctas)
     pg.ensure()
     return pg
 

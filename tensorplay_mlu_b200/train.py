@@ -39,6 +39,7 @@ tensorplay_mlu/distributed.py:241-242 does.
 
 from __future__ import annotations
 
+import contextlib
 import math
 import os
 from dataclasses import dataclass
@@ -65,10 +66,18 @@ class MLPConfig:
     # slice ahead of that step's first product (call flush() after the last
     # step).  False: every step ends with its parameters updated.
     overlap_next_step: bool = False
-    # Data-parallel: SMs left free for the collective's kernels while the
-    # d_h product overlaps bucket A's all-reduce.  0 (default): the product
-    # takes every SM, its tiles claimed at run time.
-    comm_sms: int = 0
+    # Data-parallel: SMs left free for the collective's kernels by every
+    # product that runs while an all-reduce is in flight (d_h, the dW1
+    # slices, the next step's h slices).  The products are persistent and
+    # hold one CTA per SM, so without a reserve the collective's kernels
+    # find no SM until a product ends; the process group is created with
+    # its collectives bounded to as many CTAs (create(max_ctas=...)).
+    # 0: the products take every SM.
+    comm_sms: int = 16
+    # Data-parallel: those products claim their tiles at run time
+    # (tp_b200_set_gemm_tile_order), so clusters that start late behind the
+    # collective's kernels take fewer tiles.
+    comm_dynamic_tiles: bool = False
 
 
 def init_params_host(cfg: MLPConfig, seed: int = 0):
@@ -127,11 +136,20 @@ class DataParallelMLP:
         self.w1 = self.params_b.narrow(0, H, H * D).view(H, D)
         for dst, src in ((self.w1, w1), (self.b1, b1), (self.w2, w2), (self.b2, b2)):
             ops.copy_(dst, ops.to_device(src.contiguous(), dev))
-        self.comm_stream = torch.cuda.Stream(device=dev) if pg is not None and self.world > 1 else None
-        # TPB200_COMM_SMS overrides cfg.comm_sms (A/B measurements).
+        # The exchange runs on a high-priority stream, so when SMs free up the
+        # collective's CTAs are dispatched ahead of the compute stream's
+        # (TPB200_COMM_PRIORITY=0: default priority, for A/B measurements).
+        prio = -1 if os.environ.get("TPB200_COMM_PRIORITY", "1") != "0" else 0
+        self.comm_stream = (torch.cuda.Stream(device=dev, priority=prio)
+                            if pg is not None and self.world > 1 else None)
+        # TPB200_COMM_SMS / TPB200_COMM_DYNAMIC override cfg.comm_sms /
+        # cfg.comm_dynamic_tiles (A/B measurements).
         reserve = int(os.environ.get("TPB200_COMM_SMS", cfg.comm_sms))
         total = torch.cuda.get_device_properties(dev).multi_processor_count
         self._overlap_sms = total - reserve if self.comm_stream is not None and 0 < reserve < total else 0
+        dyn = os.environ.get("TPB200_COMM_DYNAMIC")
+        self._overlap_dynamic = self.comm_stream is not None and (
+            cfg.comm_dynamic_tiles if dyn is None else dyn not in ("", "0"))
         # When a list, every GEMM of the step appends a (start, end) pair of
         # CUDA events recorded around its launch on the current stream.
         self.gemm_events: Optional[list] = None
@@ -189,6 +207,26 @@ class DataParallelMLP:
     def _gemm_sm_limit(self, sms: int) -> None:
         N.check(N.lib().tp_b200_set_gemm_sm_limit(self.device.index, sms), "set_gemm_sm_limit")
 
+    @contextlib.contextmanager
+    def _beside_collective(self):
+        """Products launched inside run beside an all-reduce: they leave
+        comm_sms SMs free (and claim tiles at run time when configured)."""
+        if self.comm_stream is None:
+            yield
+            return
+        dev = self.device.index
+        if self._overlap_sms:
+            self._gemm_sm_limit(self._overlap_sms)
+        if self._overlap_dynamic:
+            N.check(N.lib().tp_b200_set_gemm_tile_order(dev, 1), "set_gemm_tile_order")
+        try:
+            yield
+        finally:
+            if self._overlap_sms:
+                self._gemm_sm_limit(0)
+            if self._overlap_dynamic:
+                N.check(N.lib().tp_b200_set_gemm_tile_order(dev, 0), "set_gemm_tile_order")
+
     def _allreduce_async(self, bucket, ready_event):
         """SUM all-reduce of ``bucket`` on the comm stream after ``ready_event``."""
         self.comm_stream.wait_event(ready_event)
@@ -208,7 +246,8 @@ class DataParallelMLP:
             # The previous step's bucket B, slice by slice: update the rows of
             # W1 (and b1, first slice) once their exchange is in, then the
             # columns of h and a those rows produce.
-            self._timed(self._forward_sliced, x, h, a)
+            with self._beside_collective():
+                self._timed(self._forward_sliced, x, h, a)
         else:
             self._timed(self._gemm_epilogue, N.EPI_GELU, a, h, x, self.w1.t(), self.b1)
         out = self._timed(ops.linear, a, self.w2, self.b2)
@@ -225,13 +264,7 @@ class DataParallelMLP:
             work_a = self._allreduce_async(self.bucket_a, ev)
         # d_h = gelu_backward(d_out W2, h) from one product
         d_h = torch.empty((B, H), dtype=dt, device=dev)
-        if self._overlap_sms:
-            self._gemm_sm_limit(self._overlap_sms)
-            try:
-                self._timed(self._gemm_epilogue, N.EPI_GELU_BACKWARD, d_h, h, d_out, self.w2)
-            finally:
-                self._gemm_sm_limit(0)
-        else:
+        with self._beside_collective():
             self._timed(self._gemm_epilogue, N.EPI_GELU_BACKWARD, d_h, h, d_out, self.w2)
         if self.trace is not None:
             self.trace.update(x=x, t=target, h=h, a=a, out=out, d_out=d_out, d_h=d_h, loss=loss)
@@ -244,7 +277,8 @@ class DataParallelMLP:
         # Bucket B in row slices of dW1 (db1 travels with the first); each
         # slice's SUM all-reduce starts once its product is done.
         self._colsum_into(self.db1, d_h)
-        pending = self._dw1_sliced(d_h, x)
+        with self._beside_collective():
+            pending = self._dw1_sliced(d_h, x)
         # SGD: p += (-lr / world) * g_sum, bucket A as soon as it is in.
         work_a.wait()
         ops.add__Tensor(self.params_a, self.bucket_a, alpha=self._sgd_scale())

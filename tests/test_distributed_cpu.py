@@ -43,9 +43,9 @@ class FakeNccl:
         ctypes.memmove(buf, bytes((i * 7 + 3) % 256 for i in range(self.ID_BYTES)), self.ID_BYTES)
         return 0
 
-    def tp_b200_nccl_comm_init_timeout(self, rank, nranks, dev, buf, timeout_ms, comm_ref):
+    def tp_b200_nccl_comm_init_ctas(self, rank, nranks, dev, buf, timeout_ms, min_ctas, max_ctas, comm_ref):
         self.seen_id = bytes(buf.raw[: self.ID_BYTES])
-        self.init_args = (rank, nranks, dev, timeout_ms)
+        self.init_args = (rank, nranks, dev, timeout_ms, max_ctas)
         return 0
 
     def tp_b200_nccl_last_error(self):
@@ -65,7 +65,7 @@ def _worker(rank: int, port: int, out_dir: str) -> None:
     got_max = host.max(float(rank) + 0.5)
     host.barrier()
     pg = D.ProcessGroupB200(bench._PrefixStore("nccl_b200", host.store), rank, 2, device=rank,
-                            group_name="g", timeout_s=30)
+                            group_name="g", timeout_s=30, max_ctas=16)
     pg.ensure()
     host.barrier()
     host.close()
@@ -85,7 +85,7 @@ def test_rendezvous_and_host_group_with_two_gloo_ranks(tmp_path):
     r0, r1 = torch.load(tmp_path / "r0.pt"), torch.load(tmp_path / "r1.pt")
     assert r0["max"] == r1["max"] == 1.5
     assert r0["id"] == r1["id"] and len(r0["id"]) == FakeNccl.ID_BYTES
-    assert r0["args"] == (0, 2, 0, 30000) and r1["args"] == (1, 2, 1, 30000)
+    assert r0["args"] == (0, 2, 0, 30000, 16) and r1["args"] == (1, 2, 1, 30000, 16)
 
 
 def test_rank_without_rendezvous_times_out():
@@ -114,7 +114,7 @@ def test_native_errors_surface_as_exceptions():
     from tensorplay_mlu_b200 import distributed as D
 
     class Failing(FakeNccl):
-        def tp_b200_nccl_comm_init_timeout(self, *args):
+        def tp_b200_nccl_comm_init_ctas(self, *args):
             return -1
 
         def tp_b200_nccl_last_error(self):
