@@ -62,10 +62,17 @@ class MLPConfig:
     # all-reduced in this many row slices of dW1, so each slice's exchange
     # overlaps the next slice's product.
     dw1_slices: int = 2
-    # Data-parallel: defer bucket B's SGD update into the next step, slice by
-    # slice ahead of that step's first product (call flush() after the last
-    # step).  False: every step ends with its parameters updated.
+    # Data-parallel: defer an exchange's SGD update into the next step (call
+    # flush() after the last step).  False: every step ends with its
+    # parameters updated.
     overlap_next_step: bool = False
+    # Data-parallel order of the backward products.  "w1_first": d_h, dW1
+    # (bucket B exchanged beside dW2), then dW2 (bucket A exchanged beside
+    # the next step's first product, applied before its second).
+    # "w2_first": dW2 (bucket A beside d_h and dW1), then d_h and dW1
+    # (bucket B applied slice by slice ahead of the next step's first
+    # product).  The gradients are the same either way.
+    dp_order: str = "w1_first"
     # Data-parallel: SMs left free for the collective's kernels by every
     # product that runs while an all-reduce is in flight (d_h, the dW1
     # slices, the next step's h slices).  The products are persistent and
@@ -157,6 +164,9 @@ class DataParallelMLP:
         self.trace: Optional[dict] = None
         # Bucket B slices whose SGD update is deferred: (start, length, work).
         self._pending: list = []
+        # Bucket A's exchange whose SGD update is deferred (w1_first order).
+        self._pending_a = None
+        self._order = os.environ.get("TPB200_DP_ORDER", cfg.dp_order)
         bounds = [(H * i // max(1, cfg.dw1_slices)) // 8 * 8 for i in range(max(1, cfg.dw1_slices))] + [H]
         self._slices = [(bounds[i], bounds[i + 1]) for i in range(len(bounds) - 1) if bounds[i + 1] > bounds[i]]
 
@@ -248,23 +258,30 @@ class DataParallelMLP:
             # columns of h and a those rows produce.
             with self._beside_collective():
                 self._timed(self._forward_sliced, x, h, a)
+        elif self._pending_a is not None:
+            # The previous step's bucket A is still being exchanged.
+            with self._beside_collective():
+                self._timed(self._gemm_epilogue, N.EPI_GELU, a, h, x, self.w1.t(), self.b1)
         else:
             self._timed(self._gemm_epilogue, N.EPI_GELU, a, h, x, self.w1.t(), self.b1)
+        self._apply_pending_a()  # W2, b2 before the product that reads them
         out = self._timed(ops.linear, a, self.w2, self.b2)
         # loss = mean((out - t)^2) and d out = 2 (out - t) / numel in one pass
         loss = torch.empty((), dtype=dt, device=dev)
         d_out = torch.empty_like(out)
         self._mse_into(loss, d_out, out, target)
-        self._timed(self._mm_into, self.dw2, d_out.t(), a)
-        self._colsum_into(self.db2, d_out)
         work_a = None
-        if self.comm_stream is not None:
-            ev = torch.cuda.Event()
-            ev.record()
-            work_a = self._allreduce_async(self.bucket_a, ev)
+        if self.comm_stream is None or self._order != "w1_first":
+            self._timed(self._mm_into, self.dw2, d_out.t(), a)
+            self._colsum_into(self.db2, d_out)
+            if self.comm_stream is not None:
+                ev = torch.cuda.Event()
+                ev.record()
+                work_a = self._allreduce_async(self.bucket_a, ev)
         # d_h = gelu_backward(d_out W2, h) from one product
         d_h = torch.empty((B, H), dtype=dt, device=dev)
-        with self._beside_collective():
+        beside = self._beside_collective() if work_a is not None else contextlib.nullcontext()
+        with beside:
             self._timed(self._gemm_epilogue, N.EPI_GELU_BACKWARD, d_h, h, d_out, self.w2)
         if self.trace is not None:
             self.trace.update(x=x, t=target, h=h, a=a, out=out, d_out=d_out, d_h=d_h, loss=loss)
@@ -274,11 +291,12 @@ class DataParallelMLP:
             # SGD: p += -lr * g over the whole flat buffer
             ops.add__Tensor(self.param_flat, self.grad_flat, alpha=-cfg.lr)
             return loss
+        if self._order == "w1_first":
+            return self._backward_w1_first(x, a, d_out, d_h, loss)
         # Bucket B in row slices of dW1 (db1 travels with the first); each
         # slice's SUM all-reduce starts once its product is done.
         self._colsum_into(self.db1, d_h)
-        with self._beside_collective():
-            pending = self._dw1_sliced(d_h, x)
+        pending = self._dw1_sliced(d_h, x, beside_from=0)
         # SGD: p += (-lr / world) * g_sum, bucket A as soon as it is in.
         work_a.wait()
         ops.add__Tensor(self.params_a, self.bucket_a, alpha=self._sgd_scale())
@@ -290,9 +308,35 @@ class DataParallelMLP:
     def _sgd_scale(self) -> float:
         return -self.cfg.lr / self.world
 
+    def _apply_pending_a(self) -> None:
+        if self._pending_a is not None:
+            self._pending_a.wait()
+            ops.add__Tensor(self.params_a, self.bucket_a, alpha=self._sgd_scale())
+            self._pending_a = None
+
+    def _backward_w1_first(self, x, a, d_out, d_h, loss):
+        """dW1 (bucket B's exchange beside dW2), then dW2 (bucket A's exchange
+        beside the next step's first product)."""
+        self._colsum_into(self.db1, d_h)
+        pending_b = self._dw1_sliced(d_h, x, beside_from=1)
+        with self._beside_collective():
+            self._timed(self._mm_into, self.dw2, d_out.t(), a)
+        self._colsum_into(self.db2, d_out)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._pending_a = self._allreduce_async(self.bucket_a, ev)
+        for start, length, work in pending_b:
+            work.wait()
+            ops.add__Tensor(self.params_b.narrow(0, start, length), self.bucket_b.narrow(0, start, length),
+                            alpha=self._sgd_scale())
+        if not self.cfg.overlap_next_step:
+            self._apply_pending_a()
+        return loss
+
     def flush(self) -> None:
-        """Apply the SGD update of every bucket-B slice still pending (the
-        last step's, with overlap_next_step); a no-op otherwise."""
+        """Apply every SGD update still pending (the last step's, with
+        overlap_next_step); a no-op otherwise."""
+        self._apply_pending_a()
         for start, length, work in self._pending:
             work.wait()
             ops.add__Tensor(self.params_b.narrow(0, start, length), self.bucket_b.narrow(0, start, length),
@@ -309,10 +353,11 @@ class DataParallelMLP:
             self._gemm_epilogue(N.EPI_GELU, a[:, r0:r1], h[:, r0:r1], x, self.w1[r0:r1].t(), self.b1[r0:r1])
         self._pending = []
 
-    def _dw1_sliced(self, d_h, x):
+    def _dw1_sliced(self, d_h, x, beside_from: int = 0):
         """dW1 = d_h^T x in row slices (one timed GEMM region), each slice's
-        all-reduce issued as soon as the slice is written; returns the
-        slices as (offset in bucket B, length, work)."""
+        all-reduce issued as soon as the slice is written; slices from
+        `beside_from` on run beside a collective.  Returns the slices as
+        (offset in bucket B, length, work)."""
         H = self.cfg.d_hidden
         D = self.cfg.d_in
         pending = []
@@ -321,7 +366,8 @@ class DataParallelMLP:
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             start.record()
         for i, (r0, r1) in enumerate(self._slices):
-            self._mm_into(self.dw1[r0:r1], d_h[:, r0:r1].t(), x)
+            with self._beside_collective() if i >= beside_from else contextlib.nullcontext():
+                self._mm_into(self.dw1[r0:r1], d_h[:, r0:r1].t(), x)
             ev = torch.cuda.Event()
             ev.record()
             lo = 0 if i == 0 else H + r0 * D  # db1 travels with the first slice
@@ -331,6 +377,13 @@ class DataParallelMLP:
             end.record()
             self.gemm_events.append((start, end))
         return pending
+
+    def gemm_names(self):
+        """The step's products in the order their timing events are recorded."""
+        h, o, w2, dh, w1 = ("h=xW1^T", "out=aW2^T", "dW2=dout^T a", "dh=gelu'(dout W2)", "dW1=dh^T x")
+        if self.comm_stream is not None and self._order == "w1_first":
+            return (h, o, dh, w1, w2)
+        return (h, o, w2, dh, w1)
 
     def flops_per_step(self) -> float:
         """Five GEMMs of 2 * B * D * H each (forward 2, backward 3, no dX)."""

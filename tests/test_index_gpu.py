@@ -9,7 +9,7 @@ import pytest
 import torch
 
 import oracle as O
-from conftest import assert_close, assert_equal
+from conftest import TOL, assert_close_terms, assert_equal
 
 pytestmark = pytest.mark.gpu
 
@@ -38,11 +38,35 @@ def ops(backend):
     return backend.ops
 
 
-def check(got, want, dtype, exact=False, scale=1.0):
+# Unit roundoff of each floating type (half its machine epsilon).
+UNIT = {torch.float32: 2.0 ** -24, torch.bfloat16: 2.0 ** -8, torch.float16: 2.0 ** -11, torch.float64: 2.0 ** -53}
+
+
+def check(got, want, dtype, exact=False, terms=None):
+    """Integers and exact ops bit for bit; a sum within the dtype's tolerance
+    of the magnitude of its terms (`terms`: the same op on |values|)."""
     if exact or not dtype.is_floating_point:
         assert_equal(got.cpu() if got.device.type != "cpu" else got, want)
     else:
-        assert_close(got, want, dtype, scale)
+        assert_close_terms(got, want, terms if terms is not None else want.abs(), dtype)
+
+
+def check_product(got, want, dtype, factors):
+    """A product of up to `factors` values, formed in any order with a
+    rounding after each multiply, is within gamma_n |exact| of the exact
+    product (Higham, Accuracy and Stability of Numerical Algorithms, 3.1:
+    gamma_n = n u / (1 - n u)), plus the oracle's own final rounding (u) --
+    elementwise and relative, so near-zero products need no absolute floor.
+    The accumulation in fp32 (fp64 for fp64) is rounded to the storage type
+    once more at the end."""
+    got = got.cpu().double()
+    want = want.double()
+    acc_u = UNIT[torch.float64] if dtype == torch.float64 else UNIT[torch.float32]
+    n = factors
+    gamma = n * acc_u / (1 - n * acc_u) + 2 * UNIT[dtype]
+    assert torch.equal(torch.isnan(got), torch.isnan(want))
+    ok = (got - want).abs() <= gamma * want.abs() + 1e-30
+    assert bool(ok.all()), f"max relative error {((got - want).abs() / want.abs()).max().item()} > {gamma}"
 
 
 @pytest.mark.parametrize("dtype", FLOATS + INTS + [torch.bool])
@@ -61,7 +85,8 @@ def test_gather_and_backward(ops, dtype):
         grad = values(40, 17, dtype=dtype, seed=5)
         got = ops.gather_backward(ops.to_device(grad), ops.to_device(x), 0, ops.to_device(idx))
         want = O.scatter(torch.zeros_like(x), 0, idx, grad, "add")
-        check(got, want, dtype, scale=4)
+        terms = O.scatter(torch.zeros_like(x), 0, idx, grad.abs(), "add") if dtype.is_floating_point else None
+        check(got, want, dtype, terms=terms)
 
 
 @pytest.mark.parametrize("dtype", FLOATS + INTS)
@@ -75,7 +100,8 @@ def test_index_select_and_backward(ops, dtype):
         gshape[dim] = n
         grad = values(*gshape, dtype=dtype, seed=8, lo=-5, hi=5)
         got = ops.index_select_backward(ops.to_device(grad), list(shape), dim, ops.to_device(idx))
-        check(got, O.index_add_zeros(list(shape), dim, idx, grad), dtype, scale=8)
+        terms = O.index_add_zeros(list(shape), dim, idx, grad.abs()) if dtype.is_floating_point else None
+        check(got, O.index_add_zeros(list(shape), dim, idx, grad), dtype, terms=terms)
 
 
 @pytest.mark.parametrize("dtype", FLOATS + INTS)
@@ -88,18 +114,29 @@ def test_scatter_modes(ops, dtype):
     g = torch.Generator().manual_seed(12)
     perm = torch.stack([torch.randperm(20, generator=g)[:15] for _ in range(9)], 1)
     check(ops.scatter_reduce_op(d(x), 0, d(perm), d(src)), O.scatter(x, 0, perm, src[:15]), dtype, exact=True)
-    check(ops.scatter_add(d(x), 0, d(idx), d(src)), O.scatter(x, 0, idx, src, "add"), dtype, scale=4)
+    fl = dtype.is_floating_point
+    check(ops.scatter_add(d(x), 0, d(idx), d(src)), O.scatter(x, 0, idx, src, "add"), dtype,
+          terms=O.scatter(x.abs(), 0, idx, src.abs(), "add") if fl else None)
+    # The most factors any output of a prod reduction multiplies: its own
+    # value and every source row that lands on it.
+    factors = 1 + int(torch.bincount(idx[:, 0], minlength=20).max())
+    for c in range(idx.shape[1]):
+        factors = max(factors, 1 + int(torch.bincount(idx[:, c], minlength=20).max()))
     for red in ("sum", "prod", "amax", "amin", "mean"):
         for inc in (True, False):
             got = ops.scatter_reduce(d(x), 0, d(idx), d(src), red, inc)
             want = O.scatter(x, 0, idx, src, red, inc)
-            exact = red in ("amax", "amin")
-            scale = 64 if red == "prod" else 4
-            check(got, want, dtype, exact=exact, scale=scale)
+            if red in ("amax", "amin") or not fl:
+                check(got, want, dtype, exact=True)
+            elif red == "prod":
+                check_product(got, want, dtype, factors)
+            else:
+                check(got, want, dtype, terms=O.scatter(x.abs(), 0, idx, src.abs(), red, inc))
     # In place, and the scatter.reduce spellings.
     y = d(x)
     ops.scatter_add_(y, 1, d(indices(20, 4, high=9, seed=13)), d(src[:20, :4]))
-    check(y, O.scatter(x, 1, indices(20, 4, high=9, seed=13), src[:20, :4], "add"), dtype, scale=4)
+    check(y, O.scatter(x, 1, indices(20, 4, high=9, seed=13), src[:20, :4], "add"), dtype,
+          terms=O.scatter(x.abs(), 1, indices(20, 4, high=9, seed=13), src[:20, :4].abs(), "add") if fl else None)
     y = d(x)
     ops.scatter_reduce_op_(y, 0, d(idx), d(src), "amax")
     check(y, O.scatter(x, 0, idx, src, "amax"), dtype, exact=True)
@@ -122,17 +159,21 @@ def test_cumsum_cumprod(ops, dtype):
         x = values(*shape, dtype=dtype, seed=14, lo=-3, hi=4)
         got = ops.cumsum(d(x), dim)
         want = O.scan(x, dim, False)
-        scale = (shape[dim if dim >= 0 else len(shape) + dim]) ** 0.5
-        check(got, want, dtype, scale=max(4.0, scale))
+        fl = dtype.is_floating_point
+        check(got, want, dtype, terms=O.scan(x.abs(), dim, False) if fl else None)
         xs = values(*shape, dtype=dtype, seed=15, lo=-1, hi=2)
-        if dtype.is_floating_point:
+        if fl:
             xs = (1 + xs.double() / 50).to(dtype)
         got = ops.cumprod(d(xs), dim)
-        check(got, O.scan(xs, dim, True), dtype, scale=max(4.0, scale))
+        if fl:
+            check_product(got, O.scan(xs, dim, True), dtype, shape[dim if dim >= 0 else len(shape) + dim])
+        else:
+            check(got, O.scan(xs, dim, True), dtype)
     y = d(values(6, 8, dtype=dtype, seed=16, lo=-3, hi=4))
-    want = O.scan(ops.to_host(y), 1, False)
+    yh = ops.to_host(y)
+    want = O.scan(yh, 1, False)
     ops.cumsum_(y, 1)
-    check(y, want, dtype, scale=4)
+    check(y, want, dtype, terms=O.scan(yh.abs(), 1, False) if dtype.is_floating_point else None)
 
 
 def test_int32_cumsum_wraps_like_the_host(ops):

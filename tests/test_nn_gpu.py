@@ -11,7 +11,7 @@ import pytest
 import torch
 
 import oracle as O
-from conftest import assert_close
+from conftest import assert_close, assert_close_terms
 
 pytestmark = pytest.mark.gpu
 
@@ -49,12 +49,22 @@ def test_layer_norm_forward_backward(ops, dtype, shape, norm):
         dx, dw, db = ops.native_layer_norm_backward(dev(dy), dev(x), norm, mean, rstd, dev(w), dev(b),
                                                     [True, affine, affine])
         # The oracle's backward from the same (device) statistics.
+        hm, hr = ops.to_host(mean).double(), ops.to_host(rstd).double()
         wdx, wdw, wdb = O.layer_norm_backward(dy, x, norm, ops.to_host(mean), ops.to_host(rstd), w)
-        assert_close(dx, wdx, dtype, scale=4)
+        # Term magnitudes: per row, dx = rstd (g - mean(g) - xhat mean(g xhat))
+        # with g = dy w; dw, db sum dy xhat, dy over the rows.
+        D = int(torch.tensor(norm).prod())
+        rows = x.numel() // D
+        xr = x.double().reshape(rows, D)
+        xhat = (xr - hm.reshape(rows, 1)) * hr.reshape(rows, 1)
+        g = dy.double().reshape(rows, D) * (w.double().reshape(1, D) if affine else 1.0)
+        t_dx = hr.reshape(rows, 1) * (g.abs() + g.abs().mean(1, keepdim=True)
+                                      + xhat.abs() * (g * xhat).abs().mean(1, keepdim=True))
+        assert_close_terms(dx, wdx, t_dx.reshape(x.shape), dtype)
         if affine:
-            rows = x.numel() // wdw.numel()
-            assert_close(dw, wdw, dtype, scale=max(4.0, rows ** 0.5))
-            assert_close(db, wdb, dtype, scale=max(4.0, rows ** 0.5))
+            dyr = dy.double().reshape(rows, D)
+            assert_close_terms(dw, wdw, (dyr * xhat).abs().sum(0).reshape(wdw.shape), dtype)
+            assert_close_terms(db, wdb, dyr.abs().sum(0).reshape(wdb.shape), dtype)
         else:
             assert dw is None and db is None
 
@@ -81,13 +91,16 @@ def test_nll_loss_forward_backward(ops, dtype, reduction):
             dw = ops.to_device(w) if w is not None else None
             out, total = ops.nll_loss(ops.to_device(x), ops.to_device(tt), dw, reduction, -100)
             want_out, want_total = O.nll_loss(x, tt, w, reduction, -100)
-            assert_close(out, want_out, dtype, scale=4)
-            assert_close(total, want_total, dtype, scale=4)
+            # Term magnitudes: the weighted picked log-probabilities (and
+            # weights) summed by the sum / mean reductions.
+            terms_out, _ = O.nll_loss(x.abs(), tt, w, reduction, -100)
+            assert_close_terms(out, want_out, terms_out.abs(), dtype)
+            assert_close_terms(total, want_total, want_total.abs(), dtype)
             grad = rand(n, dtype=dtype, seed=8) if reduction == 0 else torch.tensor(1.5, dtype=dtype)
             dx = ops.nll_loss_backward(ops.to_device(grad), ops.to_device(x), ops.to_device(tt), dw, reduction,
                                        -100, total)
             want_dx = O.nll_loss_backward(grad, x, tt, w, reduction, -100, want_total)
-            assert_close(dx, want_dx, dtype, scale=4)
+            assert_close(dx, want_dx, dtype)
 
 
 def test_nll_loss_target_out_of_range_sets_the_error_word(ops, backend):
@@ -170,8 +183,11 @@ def test_embedding_forward_backward(ops):
     for freq in (False, True):
         got = ops.embedding_dense_backward(ops.to_device(grad), ops.to_device(idx), 1000, 3, freq)
         want = O.index_add_zeros([1000, 64], 0, idx.reshape(-1), grad.reshape(-1, 64))
+        terms = O.index_add_zeros([1000, 64], 0, idx.reshape(-1), grad.abs().reshape(-1, 64))
         if freq:
             counts = torch.bincount(idx.reshape(-1), minlength=1000).clamp(min=1).to(torch.float32)
             want = want / counts[:, None]
+            terms = terms / counts[:, None]
         want[3] = 0
-        assert_close(got, want, torch.float32, scale=4)
+        terms[3] = 0
+        assert_close_terms(got, want, terms, torch.float32)
