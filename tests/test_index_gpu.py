@@ -51,17 +51,19 @@ def check(got, want, dtype, exact=False, terms=None):
         assert_close_terms(got, want, terms if terms is not None else want.abs(), dtype)
 
 
-def check_product(got, want, dtype, factors):
+def check_product(got, want, dtype, factors, per_step_rounding=None):
     """A product of up to `factors` values, formed in any order with a
     rounding after each multiply, is within gamma_n |exact| of the exact
     product (Higham, Accuracy and Stability of Numerical Algorithms, 3.1:
     gamma_n = n u / (1 - n u)), plus the oracle's own final rounding (u) --
     elementwise and relative, so near-zero products need no absolute floor.
-    The accumulation in fp32 (fp64 for fp64) is rounded to the storage type
-    once more at the end."""
+    `per_step_rounding` is the type each multiply rounds to: the accumulation
+    type (fp32, fp64 for fp64) for a scan, which rounds to the storage type
+    once at the end; the storage type itself for atomic scatter updates."""
     got = got.cpu().double()
     want = want.double()
-    acc_u = UNIT[torch.float64] if dtype == torch.float64 else UNIT[torch.float32]
+    step = per_step_rounding or (torch.float64 if dtype == torch.float64 else torch.float32)
+    acc_u = UNIT[step]
     n = factors
     gamma = n * acc_u / (1 - n * acc_u) + 2 * UNIT[dtype]
     assert torch.equal(torch.isnan(got), torch.isnan(want))
@@ -129,7 +131,7 @@ def test_scatter_modes(ops, dtype):
             if red in ("amax", "amin") or not fl:
                 check(got, want, dtype, exact=True)
             elif red == "prod":
-                check_product(got, want, dtype, factors)
+                check_product(got, want, dtype, factors, per_step_rounding=dtype)
             else:
                 check(got, want, dtype, terms=O.scatter(x.abs(), 0, idx, src.abs(), red, inc))
     # In place, and the scatter.reduce spellings.
