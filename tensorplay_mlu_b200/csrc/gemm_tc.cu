@@ -805,8 +805,10 @@ constexpr size_t tc2_smem_bytes() {
            1024 + 512;
 }
 
-// Tile scheduling of the CTA-pair kernel.  The leader CTA's scheduler thread
-// decides which tile the pair computes next and publishes it through a ring
+// Tile scheduling of the CTA-pair kernel.  In the fixed order every role
+// computes the sequence itself.  With run-time claims the leader CTA's
+// scheduler thread decides which tile the pair computes next and publishes
+// it through a ring
 // of kSchedDepth slots (in both CTAs' shared memory) to its consumers: both
 // CTAs' producers, the leader's MMA thread and both CTAs' epilogue warps; -1
 // ends the sequence.  Each slot's "empty" barrier (the leader's) counts
@@ -938,6 +940,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTc2Threads, 1)
     const bool leader = rank == 0;
     const int cluster_id = blockIdx.x >> 1;
     const int num_clusters = gridDim.x >> 1;
+    // Run-time claims go through the tile ring; the fixed order needs none
+    // (every role computes it), so short-K products pay no per-tile
+    // synchronisation.
+    const bool dynamic = p.sched != nullptr;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -977,13 +983,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTc2Threads, 1)
             uint32_t phase = 0;
             bool ok = true;
             for (int iter = 0; ok; ++iter) {
-                const int slot = iter % kSchedDepth;
-                if (!mbar_wait_cluster(smem_addr(&sched_full[slot]), (iter / kSchedDepth) & 1, abort_flag)) {
-                    ok = false;
-                    break;
+                int tile;
+                if (!dynamic) {
+                    tile = next_pair_tile(p, cluster_id, num_clusters, iter);
+                } else {
+                    const int slot = iter % kSchedDepth;
+                    if (!mbar_wait_cluster(smem_addr(&sched_full[slot]), (iter / kSchedDepth) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tile = sched_tile[slot];
+                    mbar_arrive_cluster(map_to_cta(smem_addr(&sched_empty[slot]), 0));
                 }
-                const int tile = sched_tile[slot];
-                mbar_arrive_cluster(map_to_cta(smem_addr(&sched_empty[slot]), 0));
                 if (tile < 0) break;
                 int b, mt, nt;
                 tile_coords_pair(p, tile, b, mt, nt, group_m);
@@ -1024,13 +1035,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTc2Threads, 1)
             constexpr uint32_t a_kstep = A_MN ? kUmmaK * 128 : 32;
             constexpr uint32_t b_kstep = B_MN ? kUmmaK * 128 : 32;
             for (int iter = 0; ok; ++iter, ++local) {
-                const int slot = iter % kSchedDepth;
-                if (!mbar_wait(smem_addr(&sched_full[slot]), (iter / kSchedDepth) & 1, abort_flag)) {
-                    ok = false;
-                    break;
+                int tile;
+                if (!dynamic) {
+                    tile = next_pair_tile(p, cluster_id, num_clusters, iter);
+                } else {
+                    const int slot = iter % kSchedDepth;
+                    if (!mbar_wait(smem_addr(&sched_full[slot]), (iter / kSchedDepth) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tile = sched_tile[slot];
+                    mbar_arrive(smem_addr(&sched_empty[slot]));
                 }
-                const int tile = sched_tile[slot];
-                mbar_arrive(smem_addr(&sched_empty[slot]));
                 if (tile < 0) break;
                 const int acc = local & 1;
                 const uint32_t acc_phase = (local >> 1) & 1;
@@ -1074,7 +1090,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTc2Threads, 1)
         }
     } else if (warp == kSchedWarp) {
         // ------------------------------------ tile scheduler (leader CTA) --
-        if (leader && lane == 0) {
+        if (leader && lane == 0 && dynamic) {
             for (int iter = 0;; ++iter) {
                 const int slot = iter % kSchedDepth;
                 if (!mbar_wait(smem_addr(&sched_empty[slot]), ((iter / kSchedDepth) & 1) ^ 1, abort_flag)) {
@@ -1105,14 +1121,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTc2Threads, 1)
         const uint32_t leader_empty0 = map_to_cta(smem_addr(&acc_empty[0]), 0);
         const uint32_t leader_empty1 = map_to_cta(smem_addr(&acc_empty[1]), 0);
         for (int iter = 0;; ++iter, ++local) {
-            const int slot = iter % kSchedDepth;
-            if (!mbar_wait_cluster(smem_addr(&sched_full[slot]), (iter / kSchedDepth) & 1, abort_flag)) {
-                if (lane == 0) atomicExch(p.err, kErrEpilogue);
-                break;
+            int tile;
+            if (!dynamic) {
+                tile = next_pair_tile(p, cluster_id, num_clusters, iter);
+            } else {
+                const int slot = iter % kSchedDepth;
+                if (!mbar_wait_cluster(smem_addr(&sched_full[slot]), (iter / kSchedDepth) & 1, abort_flag)) {
+                    if (lane == 0) atomicExch(p.err, kErrEpilogue);
+                    break;
+                }
+                tile = sched_tile[slot];
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_addr(&sched_empty[slot]), 0));
             }
-            const int tile = sched_tile[slot];
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_addr(&sched_empty[slot]), 0));
             if (tile < 0) break;
             const int acc = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
