@@ -528,6 +528,22 @@ def collective_sweep(pg, host, ops, world: int, max_bytes: int = 1 << 30):
     return res
 
 
+def exchange_ms(pg, bucket, host, iters: int = 5) -> float:
+    """Milliseconds of one SUM all-reduce of `bucket` on `pg`, nothing beside
+    it (CUDA events, max over ranks)."""
+    for _ in range(2):
+        pg.allreduce([bucket], 0)
+    torch.cuda.synchronize()
+    host.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        pg.allreduce([bucket], 0)
+    e1.record()
+    e1.synchronize()
+    return host.max(e0.elapsed_time(e1) / iters)
+
+
 def h2d_only_ms(upload, copy_stream, steps: int, host) -> float:
     """Milliseconds per step of the e2e leg's host->device copies alone
     (both slots' batches, pinned memory, the copy stream), max over ranks."""
@@ -558,9 +574,11 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     hbm_peak, bf16_peak, bf16_sustained, peak_kind = peaks()
     # The training step's collectives take at most as many CTAs as the
     # products beside them leave SMs free (MLPConfig.comm_sms; TPB200_COMM_SMS).
+    # TPB200_NCCL_MAX_CTAS sets the bound apart from the reserve (A/B).
     comm_sms = int(os.environ.get("TPB200_COMM_SMS", MLPConfig.comm_sms))
+    max_ctas = int(os.environ.get("TPB200_NCCL_MAX_CTAS", comm_sms))
     pg = D.create(_PrefixStore("nccl_b200", host.store), rank, world, device=local, timeout_s=300,
-                  max_ctas=comm_sms) if world > 1 else None
+                  max_ctas=max_ctas) if world > 1 else None
 
     # Kernel-level extras (op sweep, GEMM set) at N = 1: measured before the
     # training loop by default, so their kernels run at the clocks a kernel
@@ -676,6 +694,12 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     # ---- the end-to-end ceiling: the same per-step host->device copies alone
     h2d_ms = h2d_only_ms(upload, copy_stream, args.steps, host)
 
+    # ---- one bucket's exchange alone, on the step's (CTA-bounded) communicator
+    exchange = None
+    if world > 1:
+        exchange = {"bucket_bytes": model.bucket_a.numel() * model.bucket_a.element_size(),
+                    "ms_bounded": round(exchange_ms(pg, model.bucket_a, host), 4)}
+
     # ---- data parallelism kept every rank's parameters identical
     params_identical = None
     if world > 1:
@@ -730,10 +754,11 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                                     "once (max over ranks): aggregate GB/s; the e2e step cannot be shorter "
                                     "than h2d_only_ms_per_step"},
             "dp_params_identical": params_identical,
+            "dp_exchange": exchange,
             "dp_schedule": {"dw1_slices": cfg.dw1_slices, "overlap_next_step": cfg.overlap_next_step,
                             "gemm_sms_beside_collective": model._overlap_sms or None,
                             "dynamic_tiles_beside_collective": model._overlap_dynamic,
-                            "nccl_max_ctas": comm_sms or None,
+                            "nccl_max_ctas": max_ctas or None,
                             "nccl_env": {k: v for k, v in os.environ.items() if k.startswith("NCCL_")}}
             if world > 1 else None,
             "gpu_launches": int(launches),
@@ -747,6 +772,11 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             sweep_pg = D.create(_PrefixStore("nccl_b200_sweep", host.store), rank, world, device=local,
                                 timeout_s=300, group_name="sweep")
             sweep = collective_sweep(sweep_pg, host, ops, world)
+            bucket = torch.empty(model.bucket_a.numel(), dtype=model.bucket_a.dtype, device="cuda")
+            unbounded = exchange_ms(sweep_pg, ops.zero_(bucket), host)
+            if rank == 0:
+                line["dp_exchange"]["ms_unbounded"] = round(unbounded, 4)
+            del bucket
             torch.cuda.synchronize()
             sweep_pg.destroy()
             if rank == 0:

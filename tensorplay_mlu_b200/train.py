@@ -80,7 +80,7 @@ class MLPConfig:
     # find no SM until a product ends; the process group is created with
     # its collectives bounded to as many CTAs (create(max_ctas=...)).
     # 0: the products take every SM.
-    comm_sms: int = 16
+    comm_sms: int = 24
     # Data-parallel: those products claim their tiles at run time
     # (tp_b200_set_gemm_tile_order), so clusters that start late behind the
     # collective's kernels take fewer tiles.
