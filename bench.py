@@ -58,11 +58,11 @@ def peaks():
 # A + B read once, C written once.
 GEMM_NAMES = ("h=xW1^T", "out=aW2^T", "dW2=dout^T a", "dh=gelu'(dout W2)", "dW1=dh^T x")
 GEMM_DRAM_BYTES = {
-    "h=xW1^T": 415750400 + 251609088,
-    "out=aW2^T": 1409426432 + 58553856,
-    "dW2=dout^T a": 995802624 + 123874816,
-    "dh=gelu'(dout W2)": 425874176 + 247974912,
-    "dW1=dh^T x": 1236060416 + 124142848,
+    "h=xW1^T": 1099996416,
+    "out=aW2^T": 1697812224,
+    "dW2=dout^T a": 1157644544,
+    "dh=gelu'(dout W2)": 1154491136,
+    "dW1=dh^T x": 1428218880,
 }
 GEMM_ALGORITHMIC_BYTES = {
     "h=xW1^T": (8192 * 4096 + 16384 * 4096 + 2 * 8192 * 16384 + 16384) * 2,
