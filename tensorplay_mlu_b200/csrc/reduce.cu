@@ -222,15 +222,31 @@ __global__ void __launch_bounds__(kThreads) reduce_rows(const T* __restrict__ x,
     if (split == 0 && threadIdx.x < head) acc0 = combine<A, OP>(acc0, load_as<A>(base[threadIdx.x]));
     const int64_t nvec = (R - head) / V;
     const VT* vp = reinterpret_cast<const VT*>(base + head);
-    // Four 16-byte loads in flight per thread.
+    // Eight 16-byte loads in flight per thread while at least eight
+    // vectors remain (a full-tensor reduction runs as one wave of blocks,
+    // each with tens of vectors per thread: four in flight left it
+    // latency-bound), then four.
     const int64_t S = int64_t(splits) * kThreads;
     int64_t v = int64_t(split) * kThreads + threadIdx.x;
-    for (; v + 3 * S < nvec; v += 4 * S) {
+    for (; v + 7 * S < nvec; v += 8 * S) {
+        const VT a = vp[v];
+        const VT b = vp[v + S];
+        const VT c = vp[v + 2 * S];
+        const VT d = vp[v + 3 * S];
+        const VT e = vp[v + 4 * S];
+        const VT f = vp[v + 5 * S];
+        const VT g = vp[v + 6 * S];
+        const VT h = vp[v + 7 * S];
+        fold4<A, OP>(acc0, acc1, acc2, acc3, a, b, c, d);
+        fold4<A, OP>(acc0, acc1, acc2, acc3, e, f, g, h);
+    }
+    if (v + 3 * S < nvec) {
         const VT a = vp[v];
         const VT b = vp[v + S];
         const VT c = vp[v + 2 * S];
         const VT d = vp[v + 3 * S];
         fold4<A, OP>(acc0, acc1, acc2, acc3, a, b, c, d);
+        v += 4 * S;
     }
     // The last (at most three) vectors of this thread, loaded together
     // rather than one round trip each.
@@ -692,6 +708,100 @@ __global__ void __launch_bounds__(THREADS) softmax_rows_reg(const T* __restrict_
     pdl_entry();
     const int64_t row = blockIdx.x;
     softmax_row<T, V, VPT, THREADS, LOG>(x + row * D, y + row * D, D, [] {});
+}
+
+// Rows of 16-bit elements, one warp per row: each lane holds VPL vectors of
+// V elements in registers, the max and the sum are warp shuffles (no block
+// barrier per row), and the block's warps walk rows in a grid-stride loop
+// (persistent), so an SM keeps every warp's row loads in flight while other
+// warps compute.  The arithmetic is softmax_row's (the same exp and
+// normalisation); only the reduction trees differ.
+template <typename T, int V, int VPL, bool LOG>
+__global__ void __launch_bounds__(128) softmax_rows_warp(const T* __restrict__ x, T* __restrict__ y,
+                                                         int64_t rows, int64_t D) {
+    pdl_entry();
+    using C = typename Compute<T>::type;
+    using VT = Vec<T, V>;
+    const int lane = threadIdx.x & 31;
+    const int64_t warp0 = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    for (int64_t r = warp0; r < rows; r += warps) {
+        const T* xr = x + r * D;
+        T* yr = y + r * D;
+        C v[VPL][V];
+        VT raw[VPL];
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int64_t idx = (int64_t(k) * 32 + lane) * V;
+            if (idx < D) raw[k] = *reinterpret_cast<const VT*>(xr + idx);
+        }
+        C m = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int64_t idx = (int64_t(k) * 32 + lane) * V;
+            if (idx < D) {
+                unpack_vec(raw[k], v[k]);
+#pragma unroll
+                for (int j = 0; j < V; ++j) m = max_nan(m, v[k][j]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < V; ++j) v[k][j] = -INFINITY;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const C ml2 = m * C(kLog2e);
+        C s = 0;
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+#pragma unroll
+            for (int j = 0; j < V; ++j) {
+                const C e = sm_exp_shift<T>(v[k][j], m, ml2);
+                s += e;
+                if constexpr (!LOG) v[k][j] = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if constexpr (LOG) {
+            const C lse = sm_log<T>(s);
+#pragma unroll
+            for (int k = 0; k < VPL; ++k)
+#pragma unroll
+                for (int j = 0; j < V; ++j) v[k][j] = (v[k][j] - m) - lse;
+        } else {
+            const C inv = C(1) / s;
+#pragma unroll
+            for (int k = 0; k < VPL; ++k)
+#pragma unroll
+                for (int j = 0; j < V; ++j) v[k][j] *= inv;
+        }
+#pragma unroll
+        for (int k = 0; k < VPL; ++k) {
+            const int64_t idx = (int64_t(k) * 32 + lane) * V;
+            if (idx < D) {
+                VT o;
+                pack_vec(v[k], o);
+                *reinterpret_cast<VT*>(yr + idx) = o;
+            }
+        }
+    }
+}
+
+template <typename T, int V, int VPL, bool LOG>
+void launch_softmax_warp(T* y, const T* x, int64_t rows, int64_t D, int dev, cudaStream_t stream) {
+    auto kern = softmax_rows_warp<T, V, VPL, LOG>;
+    static int blocks_per_sm[64] = {};
+    if (blocks_per_sm[dev] == 0) {
+        int n = 0;
+        TPB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 128, 0));
+        blocks_per_sm[dev] = std::max(n, 1);
+    }
+    const int64_t want = (rows + 3) / 4;
+    const unsigned grid = static_cast<unsigned>(std::max<int64_t>(
+        1, std::min<int64_t>(want, int64_t(num_sms(dev)) * blocks_per_sm[dev])));
+    launch_pdl(kern, grid, 128, 0, stream, x, y, rows, D);
+    check_launch("softmax_rows_warp");
 }
 
 // Many rows that fit in registers: a persistent block walks rows
@@ -1298,6 +1408,14 @@ void reduce_op_dispatch(int op, const tpb_tensor& out, const tpb_tensor& x, uint
 // elements (whose per-row work is short next to the HBM latency), the
 // one-block-per-row kernel otherwise.  TPB200_SOFTMAX=ring|reg overrides the
 // choice (for A/B measurements).
+// The warp-per-row kernel for 16-bit rows of 1025-4096 elements: opt-in
+// (TPB200_SOFTMAX=warp) until it has been measured against the ring.
+bool use_softmax_warp(int64_t rows, int dev) {
+    static const char* force = std::getenv("TPB200_SOFTMAX");
+    if (rows < int64_t(num_sms(dev)) * 4) return false;
+    return force != nullptr && std::strcmp(force, "warp") == 0;
+}
+
 bool use_softmax_ring(size_t elem_size, int64_t rows, int dev) {
     static const char* force = std::getenv("TPB200_SOFTMAX");
     if (rows < int64_t(num_sms(dev)) * 2) return false;
@@ -1339,6 +1457,11 @@ void softmax_rows_launch(T* y, const T* x, int64_t rows, int64_t D, int dev, cud
     const unsigned grid = static_cast<unsigned>(rows);
     const bool vec = D % V == 0 && aligned16(x) && aligned16(y);
     const int64_t nv = D / V;
+    if (vec && sizeof(T) == 2 && nv > 128 && nv <= 512 && use_softmax_warp(rows, dev)) {
+        if (nv <= 256) launch_softmax_warp<T, V, 8, LOG>(y, x, rows, D, dev, stream);
+        else launch_softmax_warp<T, V, 16, LOG>(y, x, rows, D, dev, stream);
+        return;
+    }
     if (vec && nv <= 2048 && use_softmax_ring(sizeof(T), rows, dev)) {
         // 4096-wide 16-bit rows: 128-thread blocks, 32 elements per thread.
         // Same-box A/B ([32768, 4096] bf16, six ring stages): 128 threads
