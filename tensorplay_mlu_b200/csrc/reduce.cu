@@ -710,100 +710,6 @@ __global__ void __launch_bounds__(THREADS) softmax_rows_reg(const T* __restrict_
     softmax_row<T, V, VPT, THREADS, LOG>(x + row * D, y + row * D, D, [] {});
 }
 
-// Rows of 16-bit elements, one warp per row: each lane holds VPL vectors of
-// V elements in registers, the max and the sum are warp shuffles (no block
-// barrier per row), and the block's warps walk rows in a grid-stride loop
-// (persistent), so an SM keeps every warp's row loads in flight while other
-// warps compute.  The arithmetic is softmax_row's (the same exp and
-// normalisation); only the reduction trees differ.
-template <typename T, int V, int VPL, bool LOG>
-__global__ void __launch_bounds__(128) softmax_rows_warp(const T* __restrict__ x, T* __restrict__ y,
-                                                         int64_t rows, int64_t D) {
-    pdl_entry();
-    using C = typename Compute<T>::type;
-    using VT = Vec<T, V>;
-    const int lane = threadIdx.x & 31;
-    const int64_t warp0 = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
-    for (int64_t r = warp0; r < rows; r += warps) {
-        const T* xr = x + r * D;
-        T* yr = y + r * D;
-        C v[VPL][V];
-        VT raw[VPL];
-#pragma unroll
-        for (int k = 0; k < VPL; ++k) {
-            const int64_t idx = (int64_t(k) * 32 + lane) * V;
-            if (idx < D) raw[k] = *reinterpret_cast<const VT*>(xr + idx);
-        }
-        C m = -INFINITY;
-#pragma unroll
-        for (int k = 0; k < VPL; ++k) {
-            const int64_t idx = (int64_t(k) * 32 + lane) * V;
-            if (idx < D) {
-                unpack_vec(raw[k], v[k]);
-#pragma unroll
-                for (int j = 0; j < V; ++j) m = max_nan(m, v[k][j]);
-            } else {
-#pragma unroll
-                for (int j = 0; j < V; ++j) v[k][j] = -INFINITY;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, o));
-        const C ml2 = m * C(kLog2e);
-        C s = 0;
-#pragma unroll
-        for (int k = 0; k < VPL; ++k) {
-#pragma unroll
-            for (int j = 0; j < V; ++j) {
-                const C e = sm_exp_shift<T>(v[k][j], m, ml2);
-                s += e;
-                if constexpr (!LOG) v[k][j] = e;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if constexpr (LOG) {
-            const C lse = sm_log<T>(s);
-#pragma unroll
-            for (int k = 0; k < VPL; ++k)
-#pragma unroll
-                for (int j = 0; j < V; ++j) v[k][j] = (v[k][j] - m) - lse;
-        } else {
-            const C inv = C(1) / s;
-#pragma unroll
-            for (int k = 0; k < VPL; ++k)
-#pragma unroll
-                for (int j = 0; j < V; ++j) v[k][j] *= inv;
-        }
-#pragma unroll
-        for (int k = 0; k < VPL; ++k) {
-            const int64_t idx = (int64_t(k) * 32 + lane) * V;
-            if (idx < D) {
-                VT o;
-                pack_vec(v[k], o);
-                *reinterpret_cast<VT*>(yr + idx) = o;
-            }
-        }
-    }
-}
-
-template <typename T, int V, int VPL, bool LOG>
-void launch_softmax_warp(T* y, const T* x, int64_t rows, int64_t D, int dev, cudaStream_t stream) {
-    auto kern = softmax_rows_warp<T, V, VPL, LOG>;
-    static int blocks_per_sm[64] = {};
-    if (blocks_per_sm[dev] == 0) {
-        int n = 0;
-        TPB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 128, 0));
-        blocks_per_sm[dev] = std::max(n, 1);
-    }
-    const int64_t want = (rows + 3) / 4;
-    const unsigned grid = static_cast<unsigned>(std::max<int64_t>(
-        1, std::min<int64_t>(want, int64_t(num_sms(dev)) * blocks_per_sm[dev])));
-    launch_pdl(kern, grid, 128, 0, stream, x, y, rows, D);
-    check_launch("softmax_rows_warp");
-}
-
 // Many rows that fit in registers: a persistent block walks rows
 // blockIdx.x, +gridDim.x, ... with `stages` of them in flight as bulk copies
 // into shared memory (one mbarrier per stage), so HBM reads continue while
@@ -1408,14 +1314,6 @@ void reduce_op_dispatch(int op, const tpb_tensor& out, const tpb_tensor& x, uint
 // elements (whose per-row work is short next to the HBM latency), the
 // one-block-per-row kernel otherwise.  TPB200_SOFTMAX=ring|reg overrides the
 // choice (for A/B measurements).
-// The warp-per-row kernel for 16-bit rows of 1025-4096 elements: opt-in
-// (TPB200_SOFTMAX=warp) until it has been measured against the ring.
-bool use_softmax_warp(int64_t rows, int dev) {
-    static const char* force = std::getenv("TPB200_SOFTMAX");
-    if (rows < int64_t(num_sms(dev)) * 4) return false;
-    return force != nullptr && std::strcmp(force, "warp") == 0;
-}
-
 bool use_softmax_ring(size_t elem_size, int64_t rows, int dev) {
     static const char* force = std::getenv("TPB200_SOFTMAX");
     if (rows < int64_t(num_sms(dev)) * 2) return false;
@@ -1457,18 +1355,15 @@ void softmax_rows_launch(T* y, const T* x, int64_t rows, int64_t D, int dev, cud
     const unsigned grid = static_cast<unsigned>(rows);
     const bool vec = D % V == 0 && aligned16(x) && aligned16(y);
     const int64_t nv = D / V;
-    if (vec && sizeof(T) == 2 && nv > 128 && nv <= 512 && use_softmax_warp(rows, dev)) {
-        if (nv <= 256) launch_softmax_warp<T, V, 8, LOG>(y, x, rows, D, dev, stream);
-        else launch_softmax_warp<T, V, 16, LOG>(y, x, rows, D, dev, stream);
-        return;
-    }
     if (vec && nv <= 2048 && use_softmax_ring(sizeof(T), rows, dev)) {
         // 4096-wide 16-bit rows: 128-thread blocks, 32 elements per thread.
         // Same-box A/B ([32768, 4096] bf16, six ring stages): 128 threads
         // 0.87-0.89 of the HBM copy peak, 256 threads 0.81-0.83, 512
         // threads 0.64 -- the per-row block reductions' barriers, not
         // occupancy, set the rate; shallower rings (3-4 stages) lost
-        // whatever the block size.
+        // whatever the block size.  A persistent warp-per-row kernel (row
+        // in registers, shuffle-only reductions, no block barrier) measured
+        // 0.77 against 0.93 for this kernel on one box and was not kept.
         if (nv <= 256) launch_ring<T, V, 1, 256, LOG>(y, x, rows, D, dev, stream);
         else if (nv <= 512) launch_ring<T, V, 4, 128, LOG>(y, x, rows, D, dev, stream);
         else if (nv <= 1024) launch_ring<T, V, 4, 256, LOG>(y, x, rows, D, dev, stream);
