@@ -179,9 +179,11 @@ struct TcParams {
     // next_pair_tile), or in a fixed order when null.
     unsigned long long* sched;
     uint32_t epoch;
-    // L2 eviction priority (CTA-pair kernel): l2_operands 1 keeps A / B
-    // panels (evict_last); l2_stream 1 lets the epilogue's result stores
-    // and activation-input loads go first (evict_first).
+    // L2 eviction priority (CTA-pair kernel): 0 the plain (unhinted)
+    // instructions; l2_operands 1 keeps A / B panels (evict_last);
+    // l2_stream 1 lets the epilogue's result stores and activation-input
+    // loads go first (evict_first); 2 the hinted instructions with
+    // evict_normal (A/B measurements).
     int l2_operands, l2_stream;
     int* err;
 };
@@ -259,7 +261,11 @@ __device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap* ma
 // The CTA-pair form of load_operand with an L2 eviction-priority policy.
 template <int ES, bool MN, bool BATCHED>
 __device__ __forceinline__ void load_operand_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar, int mn0, int k0,
-                                                  int b, int rows, uint64_t policy) {
+                                                  int b, int rows, uint64_t policy, bool hinted) {
+    if (!hinted) {
+        load_operand<ES, MN, BATCHED, true>(dst, map, bar, mn0, k0, b, rows);
+        return;
+    }
     constexpr int kEPR = 128 / ES;
     constexpr uint32_t kChunk = kEPR * 128;
     if constexpr (MN) {
@@ -374,13 +380,13 @@ __device__ __forceinline__ void store_accumulator(const TcParams& p, uint32_t t_
 // past N).
 template <typename T>
 __device__ __forceinline__ void load_aux_chunk(const TcParams& p, const T* row, int64_t n_base, float (&z)[32],
-                                               uint64_t policy) {
+                                               uint64_t policy, bool hinted) {
     constexpr int kPer = 16 / int(sizeof(T));
     if (n_base + 32 <= p.N && (reinterpret_cast<uintptr_t>(row + n_base) & 15u) == 0) {
         const uint4* src = reinterpret_cast<const uint4*>(row + n_base);
 #pragma unroll
         for (int q = 0; q < 32 / kPer; ++q) {
-            const uint4 raw = ld_global_v4_hint(src + q, policy);
+            const uint4 raw = hinted ? ld_global_v4_hint(src + q, policy) : src[q];
             float f[kPer];
             unpack_vec(*reinterpret_cast<const Vec<T, kPer>*>(&raw), f);
 #pragma unroll
@@ -440,7 +446,8 @@ __device__ __forceinline__ void store_accumulator_tma(const TcParams& p, const C
     const T* cin = static_cast<const T*>(p.cin);
     const T* aux_row = nullptr;
     if constexpr (EPI == kEpiGeluBackward) aux_row = static_cast<const T*>(p.aux) + gm * p.saux_m;
-    const uint64_t pol = p.l2_stream ? l2_policy_evict_first() : l2_policy_evict_normal();
+    const bool hint = p.l2_stream != 0;
+    const uint64_t pol = p.l2_stream == 1 ? l2_policy_evict_first() : l2_policy_evict_normal();
     uint32_t r[2][32];
     __syncwarp();
     tmem_ld32(t_rows + col0, r[0]);
@@ -478,7 +485,7 @@ __device__ __forceinline__ void store_accumulator_tma(const TcParams& p, const C
             float d[32], z[32];
             unpack_vec(packed2, d);
             if (row_ok) {
-                load_aux_chunk<T>(p, aux_row, n_base, z, pol);
+                load_aux_chunk<T>(p, aux_row, n_base, z, pol, hint);
             } else {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) z[j] = 0.0f;
@@ -507,9 +514,15 @@ __device__ __forceinline__ void store_accumulator_tma(const TcParams& p, const C
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0 && n_base < p.N && row0 < p.M) {
-            if constexpr (BATCHED) tma_store_3d_hint(tmC, smem_addr(stage), int(n_base), int(row0), b, pol);
-            else tma_store_2d_hint(tmC, smem_addr(stage), int(n_base), int(row0), pol);
-            if constexpr (EPI == kEpiGelu) tma_store_2d_hint(tmAux, smem_addr(stage2), int(n_base), int(row0), pol);
+            if (hint) {
+                if constexpr (BATCHED) tma_store_3d_hint(tmC, smem_addr(stage), int(n_base), int(row0), b, pol);
+                else tma_store_2d_hint(tmC, smem_addr(stage), int(n_base), int(row0), pol);
+                if constexpr (EPI == kEpiGelu) tma_store_2d_hint(tmAux, smem_addr(stage2), int(n_base), int(row0), pol);
+            } else {
+                if constexpr (BATCHED) tma_store_3d(tmC, smem_addr(stage), int(n_base), int(row0), b);
+                else tma_store_2d(tmC, smem_addr(stage), int(n_base), int(row0));
+                if constexpr (EPI == kEpiGelu) tma_store_2d(tmAux, smem_addr(stage2), int(n_base), int(row0));
+            }
             bulk_commit_group();
         }
     }
@@ -978,7 +991,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTc2Threads, 1)
     if (warp == 0) {
         // ---------------------------------------------------- producer --
         if (lane == 0) {
-            const uint64_t pol_ops = p.l2_operands ? l2_policy_evict_last() : l2_policy_evict_normal();
+            const bool hint_ops = p.l2_operands != 0;
+            const uint64_t pol_ops = p.l2_operands == 1 ? l2_policy_evict_last() : l2_policy_evict_normal();
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
@@ -1013,8 +1027,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTc2Threads, 1)
                     const uint32_t da = smem_addr(smem_a + stage * kABytes);
                     const uint32_t db = smem_addr(smem_b + stage * kBBytes);
                     const int k0 = kb * kEPR;
-                    load_operand_pair<E::kES, A_MN, BATCHED>(da, &tmA, fb, m0, k0, b, 128, pol_ops);
-                    load_operand_pair<E::kES, B_MN, BATCHED>(db, &tmB, fb, n0, k0, b, 128, pol_ops);
+                    load_operand_pair<E::kES, A_MN, BATCHED>(da, &tmA, fb, m0, k0, b, 128, pol_ops, hint_ops);
+                    load_operand_pair<E::kES, B_MN, BATCHED>(db, &tmB, fb, n0, k0, b, 128, pol_ops, hint_ops);
                     if (++stage == kStages) {
                         stage = 0;
                         phase ^= 1;
@@ -1375,10 +1389,11 @@ void launch_tc2(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
         const char* e = std::getenv("TPB200_GEMM_L2HINT");
         if (e == nullptr || std::strcmp(e, "none") == 0) return 0;
         if (std::strcmp(e, "both") == 0) return 2;
+        if (std::strcmp(e, "normal") == 0) return 3;
         return 1;
     }();
-    tp.l2_stream = l2hint >= 1 ? 1 : 0;
-    tp.l2_operands = l2hint >= 2 ? 1 : 0;
+    tp.l2_stream = l2hint == 3 ? 2 : l2hint >= 1 ? 1 : 0;
+    tp.l2_operands = l2hint == 3 ? 2 : l2hint == 2 ? 1 : 0;
     launch_pdl(kern, 2 * clusters, kTc2Threads, smem, stream, ma, mb, mc, maux != nullptr ? *maux : mc, tp, group_m);
     check_launch("gemm_tc2");
 }
