@@ -110,6 +110,24 @@ def make_batch_host(cfg: MLPConfig, seed: int):
     return x, t
 
 
+def bucket_b_slices(d_in: int, d_hidden: int, slices: int):
+    """The row slices bucket B = (db1 [H], dW1 [H, D]) is exchanged in:
+    [(r0, r1, offset, length)] -- dW1 rows [r0, r1) and the slice's span of
+    the flat bucket (db1 travels with the first).  Row bounds are multiples
+    of 8, so every slice of d_h's columns starts on a 16-byte boundary."""
+    H, D = d_hidden, d_in
+    n = max(1, int(slices))
+    bounds = [(H * i // n) // 8 * 8 for i in range(n)] + [H]
+    out = []
+    for i in range(n):
+        r0, r1 = bounds[i], bounds[i + 1]
+        if r1 <= r0:
+            continue
+        lo = 0 if not out else H + r0 * D
+        out.append((r0, r1, lo, H + r1 * D - lo))
+    return out
+
+
 class DataParallelMLP:
     """Parameters, gradient buckets and the training step of one rank."""
 
@@ -167,8 +185,8 @@ class DataParallelMLP:
         # Bucket A's exchange whose SGD update is deferred (w1_first order).
         self._pending_a = None
         self._order = os.environ.get("TPB200_DP_ORDER", cfg.dp_order)
-        bounds = [(H * i // max(1, cfg.dw1_slices)) // 8 * 8 for i in range(max(1, cfg.dw1_slices))] + [H]
-        self._slices = [(bounds[i], bounds[i + 1]) for i in range(len(bounds) - 1) if bounds[i + 1] > bounds[i]]
+        self._bucket_b_slices = bucket_b_slices(D, H, cfg.dw1_slices)
+        self._slices = [(r0, r1) for r0, r1, _, _ in self._bucket_b_slices]
 
     def _timed(self, fn, *args):
         if self.gemm_events is None:
@@ -358,20 +376,16 @@ class DataParallelMLP:
         all-reduce issued as soon as the slice is written; slices from
         `beside_from` on run beside a collective.  Returns the slices as
         (offset in bucket B, length, work)."""
-        H = self.cfg.d_hidden
-        D = self.cfg.d_in
         pending = []
         start = end = None
         if self.gemm_events is not None:
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             start.record()
-        for i, (r0, r1) in enumerate(self._slices):
+        for i, (r0, r1, lo, length) in enumerate(self._bucket_b_slices):
             with self._beside_collective() if i >= beside_from else contextlib.nullcontext():
                 self._mm_into(self.dw1[r0:r1], d_h[:, r0:r1].t(), x)
             ev = torch.cuda.Event()
             ev.record()
-            lo = 0 if i == 0 else H + r0 * D  # db1 travels with the first slice
-            length = H + r1 * D - lo
             pending.append((lo, length, self._allreduce_async(self.bucket_b.narrow(0, lo, length), ev)))
         if start is not None:
             end.record()

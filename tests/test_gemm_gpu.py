@@ -11,7 +11,7 @@ import pytest
 import torch
 
 import oracle as O
-from conftest import TOL, assert_close, assert_close_terms, assert_equal
+from conftest import TOL, assert_close_terms, assert_equal
 
 pytestmark = pytest.mark.gpu
 

@@ -61,3 +61,24 @@ def test_reduction_table_matches_the_reference():
     # AVG is SUM plus a 1/world scale (tensorplay_mlu/distributed.py:48-58).
     assert D._REDUCTIONS[D.ReduceOp.AVG] == (0, None)
     assert D._REDUCTIONS[D.ReduceOp.MAX][0] == 2 and D._REDUCTIONS[D.ReduceOp.MIN][0] == 3
+
+
+@pytest.mark.parametrize("d_in,d_hidden,slices", [(4096, 16384, 1), (4096, 16384, 2), (4096, 16384, 4),
+                                                  (256, 512, 2), (256, 1000, 3), (64, 24, 8)])
+def test_bucket_b_slices_tile_the_bucket(d_in, d_hidden, slices):
+    # The data-parallel step exchanges bucket B = (db1, dW1) in row slices of
+    # dW1: together they cover the flat bucket exactly once, in order, db1
+    # with the first, and every slice of d_h's columns starts 16-byte aligned.
+    from tensorplay_mlu_b200.train import bucket_b_slices
+
+    parts = bucket_b_slices(d_in, d_hidden, slices)
+    assert parts[0][2] == 0
+    offset = 0
+    rows = 0
+    for r0, r1, lo, length in parts:
+        assert lo == offset and length > 0 and r0 == rows and r1 > r0
+        assert (r0 * 2) % 16 == 0  # bf16 column offset of d_h
+        offset += length
+        rows = r1
+    assert rows == d_hidden and offset == d_hidden + d_hidden * d_in
+    assert len(parts) <= slices

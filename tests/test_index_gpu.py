@@ -9,7 +9,7 @@ import pytest
 import torch
 
 import oracle as O
-from conftest import TOL, assert_close_terms, assert_equal
+from conftest import assert_close_terms, assert_equal
 
 pytestmark = pytest.mark.gpu
 
