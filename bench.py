@@ -23,6 +23,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -183,6 +184,42 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
                 "sm_mhz_min": min(r[0] for r in rows), "reasons": reasons, "samples": len(rows),
                 "source": self.source}
+
+
+# ------------------------------------------------------- NCCL's choices
+
+NCCL_LOG = re.compile(r"AllReduce: (\d+) Bytes -> Algo (\w+) proto (\w+) channel\{Lo\.\.Hi\}=\{(\d+)\.\.(\d+)\}")
+
+
+def nccl_log_setup(rank: int):
+    """Point NCCL's INFO / TUNING log at a file of this rank (unless the user
+    set NCCL_DEBUG), so the line can report the algorithm NCCL chose for the
+    step's all-reduces.  Must run before the first communicator is made."""
+    if "NCCL_DEBUG" in os.environ:
+        return None
+    path = f"/tmp/tpb200_nccl_rank{rank}_{os.getpid()}.log"
+    os.environ.update(NCCL_DEBUG="INFO", NCCL_DEBUG_SUBSYS="INIT,TUNING", NCCL_DEBUG_FILE=path)
+    return path
+
+
+def nccl_choices(lines, sizes):
+    """{bytes: {"algo", "proto", "channels", "calls"}} for the all-reduces of
+    the given sizes, from NCCL TUNING lines; plus whether NVLS was available."""
+    out = {}
+    nvls = False
+    for line in lines:
+        if "NVLS multicast support is available" in line:
+            nvls = True
+        m = NCCL_LOG.search(line)
+        if m is None or int(m.group(1)) not in sizes:
+            continue
+        key = str(int(m.group(1)))
+        entry = out.setdefault(key, {"algo": m.group(2), "proto": m.group(3),
+                                     "channels": int(m.group(5)) - int(m.group(4)) + 1, "calls": 0})
+        entry["calls"] += 1
+        if entry["algo"] != m.group(2) or entry["proto"] != m.group(3):
+            entry["algo"], entry["proto"] = "mixed", "mixed"
+    return {"nvls_available": nvls, "allreduce": out}
 
 
 # ----------------------------------------------------------- distributed
@@ -528,6 +565,23 @@ def collective_sweep(pg, host, ops, world: int, max_bytes: int = 1 << 30):
     return res
 
 
+def nccl_summary(path, model):
+    """NCCL's algorithm / protocol / channels for the step's exchanges, from
+    this rank's log (None when the log was not ours to read)."""
+    if path is None:
+        return None
+    try:
+        with open(path, errors="replace") as f:
+            lines = f.readlines()
+    except OSError:
+        return None
+    if not lines:
+        return None
+    es = model.bucket_a.element_size()
+    sizes = {model.bucket_a.numel() * es} | {length * es for _, _, _, length in model._bucket_b_slices}
+    return nccl_choices(lines, sizes)
+
+
 def exchange_ms(pg, bucket, host, iters: int = 5) -> float:
     """Milliseconds of one SUM all-reduce of `bucket` on `pg`, nothing beside
     it (CUDA events, max over ranks)."""
@@ -570,6 +624,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     assert tpb.allocator_installed(), "the B200 caching allocator must back the benchmark's tensors"
     torch.cuda.set_device(local)
     ops = tpb.ops
+    nccl_log = nccl_log_setup(rank) if world > 1 else None
     host = HostGroup(rank, world)
     hbm_peak, bf16_peak, bf16_sustained, peak_kind = peaks()
     # The training step's collectives take at most as many CTAs as the
@@ -755,6 +810,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
                                     "than h2d_only_ms_per_step"},
             "dp_params_identical": params_identical,
             "dp_exchange": exchange,
+            "dp_nccl": nccl_summary(nccl_log, model) if world > 1 else None,
             "dp_schedule": {"dw1_slices": cfg.dw1_slices, "overlap_next_step": cfg.overlap_next_step,
                             "gemm_sms_beside_collective": model._overlap_sms or None,
                             "dynamic_tiles_beside_collective": model._overlap_dynamic,

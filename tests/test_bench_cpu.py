@@ -40,3 +40,22 @@ def test_clock_summary_from_nvml_flags():
     s.source = "nvml"
     s.rows = [(1965.0, 1965.0, [False, False, False, False]), (1900.0, 1965.0, [True, False, False, False])]
     assert s.summary()["reasons"] == ["hw_slowdown"]
+
+
+def test_nccl_choices_from_tuning_lines():
+    # Lines as NCCL 2.28 writes them with NCCL_DEBUG=INFO, NCCL_DEBUG_SUBSYS=INIT,TUNING.
+    lines = [
+        "vm:774:823 [0] NCCL INFO NVLS multicast support is available on dev 0 (NVLS_NCHANNELS 16)",
+        "vm:774:857 [0] NCCL INFO AllReduce: 67141632 Bytes -> Algo NVLS proto SIMPLE channel{Lo..Hi}={0..15}",
+        "vm:774:875 [0] NCCL INFO AllReduce: 67108864 Bytes -> Algo NVLS proto SIMPLE channel{Lo..Hi}={0..15}",
+        "vm:774:879 [0] NCCL INFO AllReduce: 134225920 Bytes -> Algo NVLS proto SIMPLE channel{Lo..Hi}={0..15}",
+        "vm:774:880 [0] NCCL INFO AllReduce: 134225920 Bytes -> Algo NVLS proto SIMPLE channel{Lo..Hi}={0..15}",
+        "vm:774:881 [0] NCCL INFO AllReduce: 4 Bytes -> Algo RING proto LL channel{Lo..Hi}={0..0}",
+    ]
+    got = bench.nccl_choices(lines, {134225920, 67141632, 67108864})
+    assert got["nvls_available"]
+    assert got["allreduce"]["134225920"] == {"algo": "NVLS", "proto": "SIMPLE", "channels": 16, "calls": 2}
+    assert got["allreduce"]["67108864"]["calls"] == 1 and "4" not in got["allreduce"]
+    mixed = bench.nccl_choices(lines + ["x AllReduce: 67108864 Bytes -> Algo RING proto LL channel{Lo..Hi}={0..7}"],
+                               {67108864})
+    assert mixed["allreduce"]["67108864"]["algo"] == "mixed"
