@@ -58,7 +58,8 @@ def set_device(device) -> None:
 
 @contextlib.contextmanager
 def device(index):
-    """Make ``index`` the current B200 device inside the block."""
+    """Context manager: B200 ``index`` is the current device while the
+    ``with`` body runs; the previous device is restored afterwards."""
     previous = current_device()
     set_device(index)
     try:
@@ -103,12 +104,13 @@ def reset_peak_memory_stats(device=None) -> None:
 
 
 def empty_cache() -> None:
-    """Return cached, unused device memory to the driver."""
+    """Free the caching allocator's idle blocks (cudaFree), keeping blocks
+    that tensors still hold."""
     _native.lib().tp_b200_empty_cache()
 
 
 def mem_get_info(device=None) -> tuple[int, int]:
-    """(free, total) bytes on the device, as the driver reports them."""
+    """cudaMemGetInfo for the device: a (free_bytes, total_bytes) tuple."""
     free = ctypes.c_size_t()
     total = ctypes.c_size_t()
     _native.check(_native.lib().tp_b200_mem_get_info(_index(device), ctypes.byref(free),
