@@ -192,10 +192,14 @@ NCCL_LOG = re.compile(r"AllReduce: (\d+) Bytes -> Algo (\w+) proto (\w+) channel
 
 
 def nccl_log_setup(rank: int):
-    """Point NCCL's INFO / TUNING log at a file of this rank (unless the user
-    set NCCL_DEBUG), so the line can report the algorithm NCCL chose for the
-    step's all-reduces.  Must run before the first communicator is made."""
-    if "NCCL_DEBUG" in os.environ:
+    """Point NCCL's INFO / TUNING log at a file of this rank, so the line can
+    report the algorithm NCCL chose for the step's all-reduces.  A quiet level
+    the environment already sets (VERSION, WARN) is replaced, since the log
+    goes to a file rather than the console; a user who asked for INFO or TRACE
+    themselves, or who set NCCL_DEBUG_FILE, keeps their own log and the line
+    reports nothing.  Must run before the first communicator is made."""
+    level = os.environ.get("NCCL_DEBUG", "").strip().upper()
+    if level not in ("", "VERSION", "WARN") or "NCCL_DEBUG_FILE" in os.environ:
         return None
     path = f"/tmp/tpb200_nccl_rank{rank}_{os.getpid()}.log"
     os.environ.update(NCCL_DEBUG="INFO", NCCL_DEBUG_SUBSYS="INIT,TUNING", NCCL_DEBUG_FILE=path)

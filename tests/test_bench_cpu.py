@@ -1,7 +1,12 @@
 """bench.py's host-side logic: the op sweep's median over full passes and
-its spread figure, and the clock summary's throttle reasons (no GPU)."""
+its spread figure, the clock summary's throttle reasons, and the NCCL log
+that reports the exchange's algorithm (no GPU)."""
 
 from __future__ import annotations
+
+import os
+
+import pytest
 
 import bench
 
@@ -59,3 +64,26 @@ def test_nccl_choices_from_tuning_lines():
     mixed = bench.nccl_choices(lines + ["x AllReduce: 67108864 Bytes -> Algo RING proto LL channel{Lo..Hi}={0..7}"],
                                {67108864})
     assert mixed["allreduce"]["67108864"]["algo"] == "mixed"
+
+
+@pytest.mark.parametrize("env,takes_over", [
+    ({}, True),
+    ({"NCCL_DEBUG": "VERSION"}, True),   # a quiet level set by the environment
+    ({"NCCL_DEBUG": "warn"}, True),
+    ({"NCCL_DEBUG": "INFO"}, False),     # the user reads NCCL's log themselves
+    ({"NCCL_DEBUG": "TRACE"}, False),
+    ({"NCCL_DEBUG": "VERSION", "NCCL_DEBUG_FILE": "/tmp/mine.%h.%p"}, False),
+])
+def test_nccl_log_setup_respects_a_user_log(monkeypatch, env, takes_over):
+    for key in ("NCCL_DEBUG", "NCCL_DEBUG_FILE", "NCCL_DEBUG_SUBSYS"):
+        monkeypatch.delenv(key, raising=False)
+    for key, value in env.items():
+        monkeypatch.setenv(key, value)
+    path = bench.nccl_log_setup(3)
+    if takes_over:
+        assert path is not None and "rank3" in path
+        assert os.environ["NCCL_DEBUG"] == "INFO" and os.environ["NCCL_DEBUG_FILE"] == path
+        assert "TUNING" in os.environ["NCCL_DEBUG_SUBSYS"]
+    else:
+        assert path is None
+        assert os.environ["NCCL_DEBUG"] == env["NCCL_DEBUG"]
