@@ -54,8 +54,10 @@ def peaks():
 
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of
 # each of the step's five products, from one ncu capture of the five
-# gemm_tc2_kernel launches of a full-size step (the command and the figures:
-# profiles/gemm_tc2_mlp_step_5_products.md).  Algorithmic bytes per launch:
+# gemm_tc2_kernel launches of a full-size step (`ncu --metrics
+# dram__bytes_read.sum,dram__bytes_write.sum --clock-control none -k
+# regex:gemm_tc2 -s 5 -c 5` of `bench.py --only mlp_step --steps 2`; its
+# summary is kept with the profiles).  Algorithmic bytes per launch:
 # A + B read once, C written once.
 GEMM_NAMES = ("h=xW1^T", "out=aW2^T", "dW2=dout^T a", "dh=gelu'(dout W2)", "dW1=dh^T x")
 GEMM_DRAM_BYTES = {
@@ -473,8 +475,10 @@ def quick_start(ops, iters: int = 200):
                     "times per chain on the stream, eager_wall_ms the host wall clock"}
 
 
-def gemm_set(ops, bf16_peak: float):
-    """achieved TFLOP/s of the GEMM shapes."""
+def gemm_set(ops, bf16_peak: float, hbm_peak: float = None):
+    """achieved TFLOP/s of the GEMM shapes; for the bmm
+    (K = 128, below the ridge: bound by HBM) also its algorithmic bytes --
+    A, B and C once each -- per second against the HBM copy peak."""
     g = torch.Generator(device="cuda").manual_seed(0)
     res = {}
 
@@ -500,8 +504,10 @@ def gemm_set(ops, bf16_peak: float):
     ba, bb = rnd(64, 2048, 128, k=128), rnd(64, 128, 2048, k=128)
     ms = time_events(lambda: ops.bmm(ba, bb), 10)
     record("bmm_64x2048x128x2048_bf16", ms, 2 * 64 * 2048 * 128 * 2048, bf16_peak)
-    bytes_bmm = (64 * 2048 * 128 * 2 + 64 * 128 * 2048 + 64 * 2048 * 2048) * 2
-    res["bmm_64x2048x128x2048_bf16"]["hbm_gb_s"] = round(bytes_bmm / (ms * 1e-3) / 1e9, 1)
+    bytes_bmm = (64 * 2048 * 128 + 64 * 128 * 2048 + 64 * 2048 * 2048) * 2
+    gbs = bytes_bmm / (ms * 1e-3) / 1e9
+    res["bmm_64x2048x128x2048_bf16"].update(
+        bound="hbm", hbm_gb_s=round(gbs, 1), hbm_frac=round(gbs / hbm_peak, 3) if hbm_peak else None)
     del ba, bb
     n = 4096
     fa, fb = rnd(n, n, k=n, dt=torch.float32), rnd(n, n, k=n, dt=torch.float32)
@@ -646,7 +652,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
     if world == 1 and not args.no_extras and args.extras_order == "first":
         with ClockSampler(local) as extra_clocks:
             pre["op_sweep"] = op_sweep(ops, hbm_peak)
-            pre["gemm_set"] = gemm_set(ops, bf16_peak)
+            pre["gemm_set"] = gemm_set(ops, bf16_peak, hbm_peak)
             pre["quick_start"] = quick_start(ops)
         pre["extras_clocks"] = extra_clocks.summary()
         torch.cuda.empty_cache()
@@ -857,7 +863,7 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
         else:
             with ClockSampler(local) as extra_clocks:
                 line["op_sweep"] = op_sweep(ops, hbm_peak)
-                line["gemm_set"] = gemm_set(ops, bf16_peak)
+                line["gemm_set"] = gemm_set(ops, bf16_peak, hbm_peak)
                 line["quick_start"] = quick_start(ops)
             line["extras_clocks"] = extra_clocks.summary()
         cpu_value, threads, _, gflops = cpu_mlp_throughput(2, 1)
@@ -994,7 +1000,7 @@ def main() -> None:
         import tensorplay_mlu_b200 as tpb
 
         tpb.load()
-        print(json.dumps({"gemm_set": gemm_set(tpb.ops, peaks()[1])}), flush=True)
+        print(json.dumps({"gemm_set": gemm_set(tpb.ops, peaks()[1], peaks()[0])}), flush=True)
         return
     if args.sweep_only:
         import tensorplay_mlu_b200 as tpb

@@ -30,9 +30,11 @@ the next slice's product.  With `overlap_next_step` the SGD update of
 bucket B's slices is deferred into the next step, each slice applied just
 before the next step's h = x W1^T product for the same rows of W1, which
 runs slice by slice -- so no exchange waits after the last product of a
-step; `flush()` applies what is still pending.  The tensor-core products
-claim their tiles at run time, so SMs taken by the collective's kernels
-delay no tiles.  The AVG's 1/world scale is folded into the SGD step
+step; `flush()` applies what is still pending.  Every product that runs
+while an exchange is in flight leaves `comm_sms` SMs to the collective's
+kernels (the communicator is bounded to as many CTAs), and with
+`comm_dynamic_tiles` claims its tiles at run time instead of in a fixed
+order.  The AVG's 1/world scale is folded into the SGD step
 (p -= lr/world * g_sum), not launched as its own pass as
 tensorplay_mlu/distributed.py:241-242 does.
 """
