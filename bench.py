@@ -821,7 +821,9 @@ def run_ours(args, rank: int, world: int, local: int) -> None:
             "dp_params_identical": params_identical,
             "dp_exchange": exchange,
             "dp_nccl": nccl_summary(nccl_log, model) if world > 1 else None,
-            "dp_schedule": {"dw1_slices": cfg.dw1_slices, "overlap_next_step": cfg.overlap_next_step,
+            "dp_schedule": {"order": model._order, "dw1_slices": cfg.dw1_slices,
+                            "overlap_next_step": cfg.overlap_next_step,
+                            "beside_slices": model._beside_slices,
                             "gemm_sms_beside_collective": model._overlap_sms or None,
                             "dynamic_tiles_beside_collective": model._overlap_dynamic,
                             "nccl_max_ctas": max_ctas or None,

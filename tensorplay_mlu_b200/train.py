@@ -87,6 +87,13 @@ class MLPConfig:
     # (tp_b200_set_gemm_tile_order), so clusters that start late behind the
     # collective's kernels take fewer tiles.
     comm_dynamic_tiles: bool = False
+    # Data-parallel (w1_first order): the products that run beside an
+    # exchange with nothing after it in the step to overlap -- the next
+    # step's h = x W1^T beside bucket A, dW2 beside bucket B's last slice --
+    # in this many row slices, only the first leaving comm_sms SMs free, so
+    # the reserve lasts about as long as the exchange rather than the whole
+    # product.  1: the whole product beside the exchange.
+    beside_slices: int = 1
 
 
 def init_params_host(cfg: MLPConfig, seed: int = 0):
@@ -128,6 +135,15 @@ def bucket_b_slices(d_in: int, d_hidden: int, slices: int):
         lo = 0 if not out else H + r0 * D
         out.append((r0, r1, lo, H + r1 * D - lo))
     return out
+
+
+def row_slices(rows: int, slices: int):
+    """[(r0, r1)]: `rows` split into `slices` parts (empty ones dropped) whose
+    bounds are multiples of 8, so a slice of a bf16 operand's columns starts
+    on a 16-byte boundary."""
+    n = max(1, int(slices))
+    bounds = [(rows * i // n) // 8 * 8 for i in range(n)] + [rows]
+    return [(bounds[i], bounds[i + 1]) for i in range(n) if bounds[i + 1] > bounds[i]]
 
 
 class DataParallelMLP:
@@ -187,6 +203,8 @@ class DataParallelMLP:
         # Bucket A's exchange whose SGD update is deferred (w1_first order).
         self._pending_a = None
         self._order = os.environ.get("TPB200_DP_ORDER", cfg.dp_order)
+        # TPB200_BESIDE_SLICES overrides cfg.beside_slices (A/B measurements).
+        self._beside_slices = int(os.environ.get("TPB200_BESIDE_SLICES", cfg.beside_slices))
         self._bucket_b_slices = bucket_b_slices(D, H, cfg.dw1_slices)
         self._slices = [(r0, r1) for r0, r1, _, _ in self._bucket_b_slices]
 
@@ -279,9 +297,9 @@ class DataParallelMLP:
             with self._beside_collective():
                 self._timed(self._forward_sliced, x, h, a)
         elif self._pending_a is not None:
-            # The previous step's bucket A is still being exchanged.
-            with self._beside_collective():
-                self._timed(self._gemm_epilogue, N.EPI_GELU, a, h, x, self.w1.t(), self.b1)
+            # The previous step's bucket A is still being exchanged: the
+            # first row slice beside it, the rest on every SM.
+            self._timed(self._forward_beside, x, h, a)
         else:
             self._timed(self._gemm_epilogue, N.EPI_GELU, a, h, x, self.w1.t(), self.b1)
         self._apply_pending_a()  # W2, b2 before the product that reads them
@@ -339,8 +357,7 @@ class DataParallelMLP:
         beside the next step's first product)."""
         self._colsum_into(self.db1, d_h)
         pending_b = self._dw1_sliced(d_h, x, beside_from=1)
-        with self._beside_collective():
-            self._timed(self._mm_into, self.dw2, d_out.t(), a)
+        self._timed(self._dw2_beside, d_out, a)
         self._colsum_into(self.db2, d_out)
         ev = torch.cuda.Event()
         ev.record()
@@ -372,6 +389,23 @@ class DataParallelMLP:
                             alpha=self._sgd_scale())
             self._gemm_epilogue(N.EPI_GELU, a[:, r0:r1], h[:, r0:r1], x, self.w1[r0:r1].t(), self.b1[r0:r1])
         self._pending = []
+
+    def _first_beside(self, i: int):
+        return self._beside_collective() if i == 0 else contextlib.nullcontext()
+
+    def _forward_beside(self, x, h, a):
+        """h = x W1^T + b1 and a = gelu(h) in `beside_slices` row slices of
+        the batch, the first beside the exchange in flight."""
+        for i, (r0, r1) in enumerate(row_slices(x.shape[0], self._beside_slices)):
+            with self._first_beside(i):
+                self._gemm_epilogue(N.EPI_GELU, a[r0:r1], h[r0:r1], x[r0:r1], self.w1.t(), self.b1)
+
+    def _dw2_beside(self, d_out, a):
+        """dW2 = d_out^T a in `beside_slices` row slices of dW2, the first
+        beside the exchange in flight."""
+        for i, (r0, r1) in enumerate(row_slices(self.cfg.d_in, self._beside_slices)):
+            with self._first_beside(i):
+                self._mm_into(self.dw2[r0:r1], d_out[:, r0:r1].t(), a)
 
     def _dw1_sliced(self, d_h, x, beside_from: int = 0):
         """dW1 = d_h^T x in row slices (one timed GEMM region), each slice's

@@ -82,3 +82,21 @@ def test_bucket_b_slices_tile_the_bucket(d_in, d_hidden, slices):
         rows = r1
     assert rows == d_hidden and offset == d_hidden + d_hidden * d_in
     assert len(parts) <= slices
+
+
+@pytest.mark.parametrize("rows,slices", [(8192, 1), (8192, 2), (4096, 2), (64, 3), (256, 3), (8, 4), (12, 2)])
+def test_row_slices_cover_the_rows_on_aligned_bounds(rows, slices):
+    # The products beside an exchange run in row slices: in order, covering
+    # every row once, each slice non-empty and starting on a multiple of 8
+    # (16 bytes of bf16); at most `slices` of them.
+    from tensorplay_mlu_b200.train import row_slices
+
+    parts = row_slices(rows, slices)
+    assert 1 <= len(parts) <= slices
+    assert parts[0][0] == 0 and parts[-1][1] == rows
+    for (a0, a1), (b0, _) in zip(parts, parts[1:]):
+        assert a1 == b0
+    for r0, r1 in parts:
+        assert r1 > r0 and r0 % 8 == 0
+    if rows % (8 * slices) == 0:
+        assert all(r1 - r0 == rows // slices for r0, r1 in parts)

@@ -88,9 +88,12 @@ def _worker(rank: int, port: int, result_dir: str) -> None:
     rs_out = [torch.zeros(1, device="cuda"), torch.zeros(2, device="cuda")]
     pg.reduce_scatter_single_coalesced(rs_out, rs_in, ReduceOp.SUM).wait()
     out["reduce_scatter_single_coalesced"] = [ops.to_host(t).tolist() for t in rs_out]
-    # two DP steps of a small MLP, in both schedules of the last bucket
-    for overlap in (False, True):
-        cfg = MLPConfig(d_in=256, d_hidden=512, batch=64, lr=0.1, dw1_slices=2, overlap_next_step=overlap)
+    # two DP steps of a small MLP, in both schedules of the last bucket, and
+    # with the products beside an exchange in two and three (ragged) row slices
+    for key, overlap, split in (("params_overlap0", False, 1), ("params_overlap1", True, 1),
+                                ("params_split2", True, 2), ("params_split3", False, 3)):
+        cfg = MLPConfig(d_in=256, d_hidden=512, batch=64, lr=0.1, dw1_slices=2, overlap_next_step=overlap,
+                        beside_slices=split)
         params = init_params_host(cfg, seed=0)
         model = DataParallelMLP(cfg, device=rank, pg=pg, host_params=params)
         xh, th = make_batch_host(cfg, seed=rank)
@@ -98,7 +101,7 @@ def _worker(rank: int, port: int, result_dir: str) -> None:
             model.step(ops.to_device(xh), ops.to_device(th))
         model.flush()
         torch.cuda.synchronize()
-        out[f"params_overlap{int(overlap)}"] = [ops.to_host(p) for p in model.params()]
+        out[key] = [ops.to_host(p) for p in model.params()]
     pg.barrier().wait()
     torch.cuda.synchronize()
     pg.destroy()
@@ -138,12 +141,15 @@ def test_two_rank_collectives_and_dp_step(backend, tmp_path):
     assert r0["reduce_scatter_single_coalesced"] == [[1.0], [0.0, 3.0]]
     assert r1["reduce_scatter_single_coalesced"] == [[3.0], [6.0, 9.0]]
     # Both ranks hold identical parameters, equal to the single-GPU steps on
-    # the concatenated batch, in both schedules.
-    for key in ("params_overlap0", "params_overlap1"):
+    # the concatenated batch, in every schedule (bit for bit across them: a
+    # row slice of a product has the bits of the same rows of the whole).
+    schedules = ("params_overlap0", "params_overlap1", "params_split2", "params_split3")
+    for key in schedules:
         for a, b in zip(r0[key], r1[key]):
             assert torch.equal(a, b)
-    for a, b in zip(r0["params_overlap0"], r0["params_overlap1"]):
-        assert torch.equal(a, b)
+    for key in schedules[1:]:
+        for a, b in zip(r0["params_overlap0"], r0[key]):
+            assert torch.equal(a, b), key
     r0["params"] = r0["params_overlap0"]
     from tensorplay_mlu_b200.train import DataParallelMLP, MLPConfig, init_params_host, make_batch_host
 
