@@ -23,18 +23,21 @@ memory-bound operators fused into their producers:
 Data parallelism (one rank per GPU): gradients live in one flat buffer split
 into two buckets in backward order, A = (dW2, db2) and B = (db1, dW1), and
 the parameters in one flat buffer of the same layout.  Each bucket is
-all-reduced (SUM) on a side stream as soon as backward has produced it:
-bucket A beside the d_h and dW1 products; bucket B in `dw1_slices` row
-slices of dW1 (db1 travels with the first), each slice's exchange beside
-the next slice's product.  With `overlap_next_step` the SGD update of
-bucket B's slices is deferred into the next step, each slice applied just
-before the next step's h = x W1^T product for the same rows of W1, which
-runs slice by slice -- so no exchange waits after the last product of a
-step; `flush()` applies what is still pending.  Every product that runs
-while an exchange is in flight leaves `comm_sms` SMs to the collective's
-kernels (the communicator is bounded to as many CTAs), and with
-`comm_dynamic_tiles` claims its tiles at run time instead of in a fixed
-order.  The AVG's 1/world scale is folded into the SGD step
+all-reduced (SUM) on a side stream as soon as backward has produced it.  In
+the default order (`dp_order = "w1_first"`) backward runs d_h, then dW1 in
+`dw1_slices` row slices (db1 travels with the first), each slice's exchange
+beside the next product, then dW2 beside bucket B's last slice; bucket B is
+applied at the end of the step, and bucket A's exchange runs beside the next
+step's h = x W1^T product (with `overlap_next_step`; `flush()` applies what
+is still pending) and is applied before out = a W2^T.  In the "w2_first"
+order dW2 comes first (bucket A beside d_h and dW1) and bucket B's slices
+are applied ahead of the next step's h product, slice by slice.  Every
+product that runs while an exchange is in flight leaves `comm_sms` SMs to
+the collective's kernels (the communicator is bounded to as many CTAs);
+the next step's h product and dW2 run in `beside_slices` row slices with
+only the first beside the exchange; with `comm_dynamic_tiles` those
+products claim their tiles at run time instead of in a fixed order.  The
+AVG's 1/world scale is folded into the SGD step
 (p -= lr/world * g_sum), not launched as its own pass as
 tensorplay_mlu/distributed.py:241-242 does.
 """
@@ -93,7 +96,7 @@ class MLPConfig:
     # in this many row slices, only the first leaving comm_sms SMs free, so
     # the reserve lasts about as long as the exchange rather than the whole
     # product.  1: the whole product beside the exchange.
-    beside_slices: int = 1
+    beside_slices: int = 2
 
 
 def init_params_host(cfg: MLPConfig, seed: int = 0):
