@@ -88,12 +88,17 @@ def _worker(rank: int, port: int, result_dir: str) -> None:
     rs_out = [torch.zeros(1, device="cuda"), torch.zeros(2, device="cuda")]
     pg.reduce_scatter_single_coalesced(rs_out, rs_in, ReduceOp.SUM).wait()
     out["reduce_scatter_single_coalesced"] = [ops.to_host(t).tolist() for t in rs_out]
-    # two DP steps of a small MLP, in both schedules of the last bucket, and
-    # with the products beside an exchange in two and three (ragged) row slices
-    for key, overlap, split in (("params_overlap0", False, 1), ("params_overlap1", True, 1),
-                                ("params_split2", True, 2), ("params_split3", False, 3)):
+    # two DP steps of a small MLP, in both schedules of the last bucket, with
+    # the products beside an exchange in two and three (ragged) row slices,
+    # and in the other backward order
+    for key, overlap, split, order in (("params_overlap0", False, 1, "w1_first"),
+                                       ("params_overlap1", True, 1, "w1_first"),
+                                       ("params_split2", True, 2, "w1_first"),
+                                       ("params_split3", False, 3, "w1_first"),
+                                       ("params_w2first0", False, 1, "w2_first"),
+                                       ("params_w2first1", True, 1, "w2_first")):
         cfg = MLPConfig(d_in=256, d_hidden=512, batch=64, lr=0.1, dw1_slices=2, overlap_next_step=overlap,
-                        beside_slices=split)
+                        beside_slices=split, dp_order=order)
         params = init_params_host(cfg, seed=0)
         model = DataParallelMLP(cfg, device=rank, pg=pg, host_params=params)
         xh, th = make_batch_host(cfg, seed=rank)
@@ -143,7 +148,8 @@ def test_two_rank_collectives_and_dp_step(backend, tmp_path):
     # Both ranks hold identical parameters, equal to the single-GPU steps on
     # the concatenated batch, in every schedule (bit for bit across them: a
     # row slice of a product has the bits of the same rows of the whole).
-    schedules = ("params_overlap0", "params_overlap1", "params_split2", "params_split3")
+    schedules = ("params_overlap0", "params_overlap1", "params_split2", "params_split3", "params_w2first0",
+                 "params_w2first1")
     for key in schedules:
         for a, b in zip(r0[key], r1[key]):
             assert torch.equal(a, b)
