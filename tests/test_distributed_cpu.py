@@ -192,3 +192,16 @@ def test_work_wait_returns_once_the_collective_completes():
     finished = []
     work = _Work(0, None, done=lambda: finished.append(1), group=_Group(), event=DoneAfter(5))
     assert work.wait(timeout=5.0) and work.is_completed() and finished == [1]
+
+
+def test_forms_nccl_does_not_offer_raise_before_touching_the_communicator():
+    # tensorplay_mlu/distributed.py:578-591: receiving from any source and the
+    # monitored barrier are refused with a RuntimeError, not an AttributeError.
+    from tensorplay_mlu_b200 import distributed as D
+
+    store = torch.distributed.TCPStore("127.0.0.1", _free_port(), 1, True)
+    pg = D.ProcessGroupB200(store, 0, 2, device=0, group_name="refusals", timeout_s=1.0)
+    with pytest.raises(RuntimeError, match="any source"):
+        pg.recv_anysource([torch.zeros(1)])
+    with pytest.raises(RuntimeError, match="monitored_barrier"):
+        pg.monitored_barrier()

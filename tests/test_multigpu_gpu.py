@@ -64,6 +64,17 @@ def _worker(rank: int, port: int, result_dir: str) -> None:
     b = ops.to_device(torch.tensor([float(rank + 7)]))
     pg.broadcast([b], 1).wait()
     out["broadcast"] = ops.to_host(b).tolist()
+    # point to point: rank 0 sends then receives, rank 1 the mirror image
+    mine = ops.to_device(torch.tensor([100.0 * (rank + 1), 100.0 * (rank + 1) + 1], dtype=torch.bfloat16))
+    theirs = torch.zeros(2, dtype=torch.bfloat16, device="cuda")
+    peer = 1 - rank
+    if rank == 0:
+        pg.send([mine], peer).wait()
+        pg.recv([theirs], peer).wait()
+    else:
+        pg.recv([theirs], peer).wait()
+        pg.send([mine], peer).wait()
+    out["p2p"] = ops.to_host(theirs).float().tolist()
     # gather / gather_single / scatter to and from rank 1, and the coalesced forms
     g_in = ops.to_device(torch.tensor([10.0 + rank, 20.0 + rank]))
     g_out = [torch.zeros(2, device="cuda") for _ in range(WORLD)]
@@ -133,6 +144,7 @@ def test_two_rank_collectives_and_dp_step(backend, tmp_path):
         assert r["gather"] == [0.0, 0.5, 1.0, 1.5]
         assert r["broadcast"] == [8.0]
     assert r0["reduce_scatter"] == [100.0, 102.0] and r1["reduce_scatter"] == [104.0, 106.0]
+    assert r0["p2p"] == [200.0, 201.0] and r1["p2p"] == [100.0, 101.0]
     assert r0["all_to_all"] == [0.0, 10.0] and r1["all_to_all"] == [1.0, 11.0]
     # tensorplay_mlu/distributed.py:328-470
     assert r1["gather_list"] == [[10.0, 20.0], [11.0, 21.0]]
