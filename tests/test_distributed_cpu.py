@@ -205,3 +205,24 @@ def test_forms_nccl_does_not_offer_raise_before_touching_the_communicator():
         pg.recv_anysource([torch.zeros(1)])
     with pytest.raises(RuntimeError, match="monitored_barrier"):
         pg.monitored_barrier()
+
+
+def test_set_timeout_bounds_the_rendezvous():
+    # The provider's set_timeout (tensorplay_mlu/distributed.py:206) takes
+    # milliseconds and bounds the wait for the communicator id.
+    from tensorplay_mlu_b200 import _native
+    from tensorplay_mlu_b200 import distributed as D
+
+    store = torch.distributed.TCPStore("127.0.0.1", _free_port(), 1, True)
+    fake = FakeNccl(1)
+    real = _native.lib
+    _native.lib = lambda: fake
+    try:
+        pg = D.ProcessGroupB200(store, 1, 2, device=0, group_name="short", timeout_s=60.0)
+        pg.set_timeout(300)
+        t0 = time.monotonic()
+        with pytest.raises(TimeoutError):
+            pg.ensure()
+        assert time.monotonic() - t0 < 10
+    finally:
+        _native.lib = real
