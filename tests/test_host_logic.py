@@ -100,3 +100,49 @@ def test_row_slices_cover_the_rows_on_aligned_bounds(rows, slices):
         assert r1 > r0 and r0 % 8 == 0
     if rows % (8 * slices) == 0:
         assert all(r1 - r0 == rows // slices for r0, r1 in parts)
+
+
+@pytest.mark.parametrize("dtype", [torch.bool, torch.uint8, torch.int8, torch.int16, torch.int32, torch.int64,
+                                   torch.float16, torch.bfloat16, torch.float32, torch.float64])
+def test_reduction_result_dtypes_match_the_host(dtype):
+    # An explicit dtype wins, else the input's (ReduceKernels.cpp:86-88); the
+    # reference sends integer inputs to the host kernels (:97-103), where a
+    # sum of integers (bool included) accumulates in int64 and mean refuses
+    # integer inputs unless a floating dtype is given -- the device path here
+    # keeps those host results.
+    from tensorplay_mlu_b200 import ops
+
+    x = torch.zeros(3, dtype=dtype)
+    assert ops._sum_dtype(x, None) == torch.sum(x).dtype
+    assert ops._sum_dtype(x, torch.float64) == torch.float64
+    if dtype.is_floating_point:
+        assert ops._mean_dtype(x, None) == torch.mean(x).dtype
+    else:
+        with pytest.raises(RuntimeError, match="could not infer output dtype"):
+            ops._mean_dtype(x, None)
+        assert ops._mean_dtype(x, torch.float32) == torch.float32
+
+
+@pytest.mark.parametrize("self_dtype,result,ok", [
+    (torch.float32, torch.float32, True), (torch.float32, torch.int64, True),
+    (torch.int64, torch.float32, False), (torch.int32, torch.bool, True),
+    (torch.bool, torch.int32, False), (torch.bfloat16, torch.float32, True),
+])
+def test_in_place_results_cast_like_the_host(self_dtype, result, ok):
+    # An in-place operator may not write a result type the output cannot
+    # hold (an integer tensor receiving a float result), as on the host.
+    from tensorplay_mlu_b200 import ops
+
+    if ok:
+        ops._check_inplace(self_dtype, result)
+    else:
+        with pytest.raises(RuntimeError, match="can't be cast"):
+            ops._check_inplace(self_dtype, result)
+
+
+def test_layer_norm_statistics_type():
+    from tensorplay_mlu_b200 import ops
+
+    assert ops._stats_dtype(torch.float64) == torch.float64
+    for dt in (torch.float32, torch.bfloat16, torch.float16):
+        assert ops._stats_dtype(dt) == torch.float32
